@@ -1,0 +1,477 @@
+#!/usr/bin/env python
+"""Benchmark of the Redshift hot path on B200: the verify-8 step of the
+64-layer model's attention/DeltaNet layers, without the projections.
+
+One step = 16 full-attention layers (verify block of 8 tokens at context
+139,264: position 139,256, each layer with its own 570 MB fp16 KV cache) +
+48 gated-DeltaNet layers (8 tokens, each with its own 3 MB fp32 state), in
+the model's layer order (every 4th layer is attention).  Reported as
+microseconds per step (lower is better).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 runs under torchrun: each rank holds a 1/N sequence shard of every
+attention layer's KV cache, attends over it, and the (partial O, LSE) pairs
+are all-gathered with NCCL and merged (one collective per attention layer);
+DeltaNet layers are replicated.  ``--impl reference`` times the CPU oracle
+(the numpy restatement of the reference's cpu_reference.py) on a bounded
+sample of the same step, on rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = 'verify-8 attn+DeltaNet µs/step at ctx 32k/139k; % HBM roofline; prefill TFLOP/s'
+UNIT = 'us/step'
+H, HKV, HD = 24, 4, 256
+HK, HV, DK = 16, 48, 128
+C = (2 * HK + HV) * DK
+LAYERS = 64
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=30)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', choices=['b200', 'reference'], default='b200')
+    ap.add_argument('--context', type=int, default=139264)
+    ap.add_argument('--tokens', type=int, default=8)
+    ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-extras', action='store_true', help='skip the 32k / prefill side measurements')
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        d = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text())
+        return float(d['hbm_gbs']), float(d['bf16_tflops']), 'measured'
+    except Exception:
+        return 6650.0, 1590.0, 'fallback'
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '100'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ''
+            self.lines = [line for line in out.splitlines() if line.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith('active'):
+                    reasons.add(name)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': [], 'samples': 0}
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ----------------------------------------------------------------------------- workload
+class Step:
+    """Device-resident buffers of the 64 layers and the per-step dispatch."""
+
+    def __init__(self, hot, context, tokens, rank, world, seed=1234):
+        import torch
+        self.torch, self.hot = torch, hot
+        self.dev = torch.device('cuda', torch.cuda.current_device())
+        self.T, self.world, self.rank = tokens, world, rank
+        self.position = context - tokens
+        P = self.position
+        self.begin = rank * P // world
+        self.rows = (rank + 1) * P // world - self.begin            # prefix rows of this shard
+        self.last = rank == world - 1                                # the shard that receives the new rows
+        cap = self.rows + (tokens if self.last else 0)
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(seed + rank)
+        f32 = dict(device=self.dev, dtype=torch.float32)
+        self.attn, self.delta = [], []
+        for layer in range(LAYERS):
+            if layer % 4 == 3:
+                kc = torch.randn((cap, HKV, HD), generator=g, device=self.dev, dtype=torch.float16)
+                vc = torch.randn((cap, HKV, HD), generator=g, device=self.dev, dtype=torch.float16)
+                self.attn.append(dict(
+                    kc=kc, vc=vc,
+                    q_gate=torch.randn((tokens, H, 2 * HD), generator=g, **f32),
+                    key=torch.randn((tokens, HKV, HD), generator=g, **f32),
+                    value=torch.randn((tokens, HKV, HD), generator=g, **f32),
+                    out=torch.empty((tokens, H, HD), **f32)))
+            else:
+                conv = torch.zeros((C, 4), **f32)
+                conv[:, 3] = 1
+                self.delta.append(dict(
+                    state=torch.randn((HV, DK, DK), generator=g, **f32) * 0.02,
+                    history=torch.zeros((3, C), **f32),
+                    qkv=torch.randn((tokens, C), generator=g, **f32).half().float(),
+                    gate=torch.randn((tokens, HV, DK), generator=g, **f32),
+                    alpha=torch.randn((tokens, HV), generator=g, **f32),
+                    beta=torch.randn((tokens, HV), generator=g, **f32),
+                    conv=conv, out=torch.empty((tokens, HV, DK), **f32)))
+        self.ones = torch.ones(HD, **f32)
+        self.decay = torch.full((HV,), -1.0, **f32)
+        self.bias = torch.zeros(HV, **f32)
+        self.norm = torch.ones(DK, **f32)
+        if world > 1:
+            need = hot.lib.qv_attention_shard_workspace(tokens, self.rows)
+            self.part = torch.empty((tokens, H, HD), **f32)
+            self.lse = torch.empty((tokens, H), **f32)
+            self.gpart = torch.empty((world, tokens, H, HD), **f32)
+            self.glse = torch.empty((world, tokens, H), **f32)
+        else:
+            need = hot.lib.qv_attention_workspace(tokens, self.position)
+        self.ws = torch.empty(max(int(need), 256), dtype=torch.uint8, device=self.dev)
+        self.launches_per_step = len(self.attn) * (3 if world == 1 else 4) + len(self.delta)
+
+    def attention_layer(self, a):
+        hot, T = self.hot, self.T
+        if self.world == 1:
+            hot.attention(a['out'], a['kc'], a['vc'], a['q_gate'], a['key'], a['value'], self.ones, self.ones,
+                          T, self.position, workspace=self.ws)
+        else:
+            import torch.distributed as dist
+            hot.attention_shard(self.part, self.lse, a['kc'], a['vc'], self.begin, self.rows, a['q_gate'],
+                                a['key'], a['value'], self.ones, self.ones, T, self.position, workspace=self.ws)
+            dist.all_gather_into_tensor(self.gpart, self.part)
+            dist.all_gather_into_tensor(self.glse, self.lse)
+            hot.attention_merge(a['out'], self.gpart, self.glse, self.world, T, a['q_gate'])
+
+    def delta_layer(self, d):
+        self.hot.delta(d['out'], d['state'], d['history'], d['qkv'], d['gate'], d['alpha'], d['beta'], d['conv'],
+                       self.decay, self.bias, self.norm, self.T, HK, HV, DK)
+
+    def run(self, events=None):
+        ai = di = 0
+        for layer in range(LAYERS):
+            if layer % 4 == 3:
+                if events is not None:
+                    events[ai][0].record()
+                self.attention_layer(self.attn[ai])
+                if events is not None:
+                    events[ai][1].record()
+                ai += 1
+            else:
+                self.delta_layer(self.delta[di])
+                di += 1
+
+    # host-side (pinned) copies of the per-step inputs and outputs, for e2e
+    def host_mirror(self):
+        torch = self.torch
+        self.h_in, self.h_out = [], []
+        for a in self.attn:
+            self.h_in.append([(a[k], a[k].cpu().pin_memory()) for k in ('q_gate', 'key', 'value')])
+            self.h_out.append((a['out'], torch.empty_like(a['out'], device='cpu').pin_memory()))
+        for d in self.delta:
+            self.h_in.append([(d[k], d[k].cpu().pin_memory()) for k in ('qkv', 'gate', 'alpha', 'beta')])
+            self.h_out.append((d['out'], torch.empty_like(d['out'], device='cpu').pin_memory()))
+        h2d = sum(h.numel() * h.element_size() for group in self.h_in for _, h in group)
+        d2h = sum(h.numel() * h.element_size() for _, h in self.h_out)
+        return h2d, d2h
+
+    def run_e2e(self):
+        for group in self.h_in:
+            for dev, host in group:
+                dev.copy_(host, non_blocking=True)
+        self.run()
+        for dev, host in self.h_out:
+            host.copy_(dev, non_blocking=True)
+
+
+def bench_b200(args):
+    import torch
+    rank = int(os.environ.get('RANK', 0))
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device('cuda', local))
+    from redshift_b200 import HotPath
+    hot = HotPath()
+    step = Step(hot, args.context, args.tokens, rank, world)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step.run()
+    torch.cuda.synchronize()
+    if hot.status():
+        raise RuntimeError('a kernel reported a timeout during warm-up')
+
+    K = args.steps
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in step.attn]
+    layer_ms = []
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        t0.record()
+        for _ in range(K):
+            step.run(events)
+            # per-layer event pairs are read back after the region; keep the last step's
+            # pairs plus a running sum through per-step synchronisation-free bookkeeping
+            layer_ms.append(events)
+            events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                      for _ in step.attn]
+        t1.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms = t0.elapsed_time(t1) / K
+    attn_ms = statistics.mean(s.elapsed_time(e) for evs in layer_ms for s, e in evs)
+    if dist is not None:
+        t = torch.tensor([ms, attn_ms], device='cuda')
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, attn_ms = t.tolist()
+    if hot.status():
+        raise RuntimeError('a kernel reported a timeout during the timed region')
+
+    # end-to-end through the public entry points with host inputs/outputs
+    e2e = None
+    if not args.no_e2e:
+        h2d, d2h = step.host_mirror()
+        for _ in range(2):
+            step.run_e2e()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(K):
+            step.run_e2e()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = e0.elapsed_time(e1) / K
+        if dist is not None:
+            t = torch.tensor([e_ms], device='cuda')
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = t.item()
+        e2e = {'value': round(e_ms * 1e3, 2), 'unit': UNIT, 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h}
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    kv_rows = step.rows + (args.tokens if step.last else 0)
+    attn_bytes = kv_rows * HKV * HD * 2 * 2
+    achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
+    roofline = {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': hbm_peak, 'unit': 'GB/s',
+                'frac': round(achieved / hbm_peak, 4), 'traffic': None,
+                'kernel': 'attention layer (prepare + split-KV fa_kernel + combine), per rank',
+                'algorithmic_bytes_per_launch': attn_bytes, 'avg_layer_ms': round(attn_ms, 5),
+                'peak_source': peak_kind}
+
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extras:
+        extras = side_measurements(hot, torch, tc_peak, hbm_peak)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.context, args.tokens)
+
+    if rank == 0:
+        line = {
+            'metric': METRIC, 'value': round(ms * 1e3, 2), 'unit': UNIT, 'n_gpus': world, 'steps': K,
+            'warmup': args.warmup, 'ms_per_step': round(ms, 5), 'higher_is_better': False,
+            'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f16 KV/operands, f32 accumulate and state',
+            'data': 'synthetic (seeded N(0,1) fp16 KV, N(0,0.02) DeltaNet state)',
+            'config': {'workload': f'verify-{args.tokens} hot-path step of the 64-layer model: 16 attention '
+                                   f'layers at context {args.context} + 48 gated-DeltaNet layers',
+                       'context': args.context, 'verify_tokens': args.tokens, 'attention_layers': 16,
+                       'delta_layers': 48, 'attention': '24 q / 4 kv heads, d256, fp16 KV',
+                       'deltanet': '16 k / 48 v heads, d128, fp32 state',
+                       'l2': 'inputs larger than L2 (9.1 GB of KV + 151 MB of state per step)',
+                       'parallelism': f'sequence-split KV x{world} (NCCL all-gather + LSE merge), '
+                                      f'DeltaNet replicated' if world > 1 else 'single GPU'},
+            'clocks': clocks.summary(),
+            'gpu_launches': step.launches_per_step * K,
+            'e2e': e2e,
+            'roofline': roofline,
+            'cpu_baseline': cpu,
+            'per_layer_us': {'attention': round(attn_ms * 1e3, 2),
+                             'delta_estimate': round((ms - 16 * attn_ms) * 1e3 / 48, 2)},
+            'extras': extras,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def side_measurements(hot, torch, tc_peak, hbm_peak):
+    """Attention at 32k, causal prefill (config 3) and DeltaNet prefill core (config 4)."""
+    res = {}
+    # config 2 at 32,768
+    step = Step(hot, 32768, 8, 0, 1, seed=77)
+    a = step.attn[0]
+    for _ in range(3):
+        step.attention_layer(a)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(20)]
+    for i in range(20):
+        a = step.attn[i % 16]
+        ev[i][0].record()
+        step.attention_layer(a)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
+    res['attention_32k_us'] = round(ms * 1e3, 2)
+    res['attention_32k_hbm_frac'] = round(32768 * 4096 / (ms * 1e-3) / 1e9 / hbm_peak, 4)
+    del step
+    torch.cuda.empty_cache()
+    # config 3: causal prefill 4096 x 24/4 heads x 256
+    L = 4096
+    g = torch.Generator(device='cuda')
+    g.manual_seed(3)
+    q = torch.randn((L, H, HD), generator=g, device='cuda', dtype=torch.float16)
+    k = torch.randn((L, HKV, HD), generator=g, device='cuda', dtype=torch.float16)
+    v = torch.randn((L, HKV, HD), generator=g, device='cuda', dtype=torch.float16)
+    out = torch.empty((L, H, HD), device='cuda', dtype=torch.float32)
+    for _ in range(3):
+        hot.prefill_attention(out, q, k, v, L)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        hot.prefill_attention(out, q, k, v, L)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 10
+    flops = 4 * H * HD * (L * (L + 1) // 2)
+    res['prefill_us'] = round(ms * 1e3, 2)
+    res['prefill_tflops'] = round(flops / (ms * 1e-3) / 1e12, 1)
+    res['prefill_tensor_frac'] = round(flops / (ms * 1e-3) / 1e12 / tc_peak, 4)
+    # config 4: DeltaNet prefill core (4096 tokens)
+    qd = torch.randn((L, HK, DK), generator=g, device='cuda', dtype=torch.float16)
+    kd = torch.randn((L, HK, DK), generator=g, device='cuda', dtype=torch.float16)
+    vd = torch.randn((L, HV, DK), generator=g, device='cuda', dtype=torch.float16)
+    al = torch.randn((L, HV), generator=g, device='cuda')
+    be = torch.randn((L, HV), generator=g, device='cuda')
+    dec = torch.full((HV,), -1.0, device='cuda')
+    bia = torch.zeros(HV, device='cuda')
+    st = torch.zeros((HV, DK, DK), device='cuda')
+    od = torch.empty((L, HV, DK), device='cuda')
+    hot.delta_core(od, st, qd, kd, vd, al, be, dec, bia, L, HK, HV, DK)
+    e0.record()
+    for _ in range(3):
+        st.zero_()
+        hot.delta_core(od, st, qd, kd, vd, al, be, dec, bia, L, HK, HV, DK)
+    e1.record()
+    torch.cuda.synchronize()
+    res['delta_prefill_4096_us'] = round(e0.elapsed_time(e1) / 3 * 1e3, 2)
+    return res
+
+
+# ----------------------------------------------------------------------------- CPU
+def cpu_sample(context, tokens, attn_layers=1, delta_layers=3, seed=4321):
+    """Time the CPU oracle on 1 attention + 3 DeltaNet layers (1/16 of a step)."""
+    import oracle
+    from oracle import inputs as I
+    a = I.attention_layer(batch=tokens, position=context - tokens, seed=seed)
+    d = [I.delta_layer(batch=tokens, seed=seed + 1 + i) for i in range(delta_layers)]
+    t = time.perf_counter()
+    for _ in range(attn_layers):
+        oracle.attention(**a)
+    for c in d:
+        oracle.delta(**c)
+    dt = time.perf_counter() - t
+    return dt * (16 / attn_layers)
+
+
+def cpu_threads():
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        return max(i.get('num_threads', 1) for i in info) if info else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(context, tokens):
+    seconds = cpu_sample(context, tokens)
+    return {'value': round(seconds * 1e6, 1), 'unit': UNIT, 'cores': cpu_threads(), 'kind': 'port',
+            'sample': f'numpy float64 restatement of cpu_reference.py on 1 attention layer (ctx {context}, '
+                      f'verify-{tokens}) + 3 DeltaNet layers = 1/16 of a step, scaled x16; '
+                      f'BLAS threads = cores; host has {os.cpu_count()} cpus'}
+
+
+def bench_reference(args):
+    rank = int(os.environ.get('RANK', 0))
+    if rank != 0:
+        return
+    for _ in range(min(args.warmup, 1)):
+        cpu_sample(args.context, args.tokens)
+    times = [cpu_sample(args.context, args.tokens) for _ in range(args.steps)]
+    value = statistics.median(times) * 1e6
+    cores = cpu_threads()
+    line = {
+        'metric': METRIC, 'value': round(value, 1), 'unit': UNIT, 'n_gpus': int(os.environ.get('WORLD_SIZE', 1)),
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(value / 1e3, 3),
+        'higher_is_better': False, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f64',
+        'data': 'synthetic (seeded N(0,1) fp16 KV, N(0,0.02) DeltaNet state)', 'impl': 'reference',
+        'config': {'workload': f'verify-{args.tokens} hot-path step of the 64-layer model: 16 attention '
+                               f'layers at context {args.context} + 48 gated-DeltaNet layers',
+                   'context': args.context, 'verify_tokens': args.tokens},
+        'cpu_baseline': {'value': round(value, 1), 'unit': UNIT, 'cores': cores, 'kind': 'port',
+                         'sample': 'CPU oracle (numpy float64 restatement of the reference cpu_reference.py; '
+                                   'the reference itself is Python and cannot travel) on 1 attention + 3 '
+                                   'DeltaNet layers per step, scaled x16 to the 64-layer step'},
+        'e2e': {'value': round(value, 1), 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        bench_reference(args)
+    else:
+        bench_b200(args)
+
+
+if __name__ == '__main__':
+    main()

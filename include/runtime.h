@@ -1,0 +1,169 @@
+#ifndef QVELOX_RUNTIME_H
+#define QVELOX_RUNTIME_H
+/* C ABI of the B200 (sm_100a) build of the Redshift hot path, libqvelox.so.
+ *
+ * Part 1 keeps the reference ABI (cristianku/redshift src/runtime.h:14-74)
+ * symbol for symbol, so qvelox/runtime.py binds this library unmodified.
+ * Part 2 is additive: entry points with no counterpart in the reference,
+ * for prefill-length blocks, device-resident (stream-ordered) calls and the
+ * multi-GPU split-KV decode.
+ *
+ * Every int-returning function returns 0 on success and -1 on failure;
+ * qv_error() then describes the failure (thread-local, cleared by the next
+ * call).  Arguments are validated before any caller buffer is read. */
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================== Part 1: the reference ABI ===================== */
+
+/* Replaces src/runtime.h:14 (thread-local message of the last failure). */
+const char *qv_error(void);
+
+/* Replace src/runtime.h:15-21.  Quantized projections are outside this
+ * build's hot path: arguments are validated exactly like the reference
+ * (kind 8/12/14, batch 1..8, width multiple of the block, 1..248320 rows),
+ * then the call fails with "quantized projections are not part of this build". */
+int qv_test_mm(float *out, const void *weights, const float *x,
+               int kind, int batch, int width, int rows);
+int qv_test_mm_fast(float *out, const void *weights, const float *x,
+               int kind, int batch, int width, int rows);
+
+/* Replaces src/runtime.h:22-23.  Weighted RMSNorm of batch rows (1..8) of
+ * width 1..17408.  Host buffers. */
+int qv_test_norm(float *out, const float *x, const float *weights,
+                 int batch, int width, float epsilon);
+
+/* Replaces src/runtime.h:25-36.  One gated-DeltaNet layer over batch 1..8
+ * tokens, host buffers.  D = 32 or 128; 1 <= key_heads <= value_heads <= 48;
+ * value_heads divisible by key_heads; C = (2*key_heads+value_heads)*D.
+ * out/gate: [batch,value_heads,D]; state (in/out): [value_heads,D,D];
+ * history (in/out): [3,C]; qkv: [batch,C]; alpha/beta: [batch,value_heads];
+ * conv: [C,4]; decay/bias: [value_heads]; norm: [D]. */
+int qv_test_delta(float *out, float *state, float *history,
+                  const float *qkv, const float *gate,
+                  const float *alpha, const float *beta,
+                  const float *conv, const float *decay,
+                  const float *bias, const float *norm,
+                  int batch, int key_heads, int value_heads, int dim,
+                  float epsilon);
+
+/* Replaces src/runtime.h:38-46.  Fixed attention: 24 query heads, 4 KV
+ * heads, head dimension 256, batch 1..8, host buffers.
+ * out: [batch,24,256]; q_gate: [batch,24,512]; key/value: [batch,4,256];
+ * q_norm/k_norm: [256].  Caches (in/out) hold IEEE float16 bits as
+ * [position+batch,4,256]; only [0,position) is read and only the appended
+ * rows [position,position+batch) are written back.
+ * 0 <= position and position+batch <= 139264. */
+int qv_test_attention(float *out, void *key_cache, void *value_cache,
+                      const float *q_gate, const float *key, const float *value,
+                      const float *q_norm, const float *k_norm,
+                      int batch, int position, float epsilon);
+
+/* Replace src/runtime.h:54-74.  Full-model evaluation needs the quantized
+ * projections and the GGUF loader, which are outside this build: qv_create
+ * validates its arguments then fails; every call on a handle fails with
+ * "null model handle"; qv_destroy(NULL) is a no-op. */
+int qv_create(void **handle, const char *path, int context, float epsilon);
+int qv_upload(void *handle, int slot, uint64_t offset, uint64_t length);
+int qv_evaluate(void *handle, const int *tokens, int batch, float *out);
+int qv_verify(void *handle, const int *tokens, int batch, float *out);
+int qv_commit(void *handle, int accepted);
+int qv_advance(void *handle, const int *tokens, int batch, int *next);
+int qv_reset(void *handle);
+int qv_checkpoint(void *handle);
+int qv_restore(void *handle);
+int qv_position(void *handle, int *position);
+void qv_destroy(void *handle);
+
+/* ===================== Part 2: additive entry points ===================== */
+
+/* Prefill-length validation entry points: the semantics, layouts and
+ * validation of qv_test_attention / qv_test_delta, for batch >= 1
+ * (attention: position+batch <= 139264; DeltaNet: batch <= 139264).  The
+ * reference reaches these blocks only as 8-token calls (qvelox/server.py:177-193). */
+int qv_test_attention_prefill(float *out, void *key_cache, void *value_cache,
+                              const float *q_gate, const float *key, const float *value,
+                              const float *q_norm, const float *k_norm,
+                              int batch, int position, float epsilon);
+int qv_test_delta_prefill(float *out, float *state, float *history,
+                          const float *qkv, const float *gate,
+                          const float *alpha, const float *beta,
+                          const float *conv, const float *decay,
+                          const float *bias, const float *norm,
+                          int batch, int key_heads, int value_heads, int dim,
+                          float epsilon);
+
+/* Device-resident attention layer: the operation k_attention performs inside
+ * the reference model loop (src/kernels.cu:575-580, called from
+ * src/runtime.cu:402-405).  All pointers are device memory; the call is
+ * asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream).
+ * The caches hold >= position+batch rows.  `workspace` is caller-owned device
+ * memory of at least qv_attention_workspace(batch, position) bytes. */
+size_t qv_attention_workspace(int batch, int position);
+int qv_attention(float *out, void *key_cache, void *value_cache,
+                 const float *q_gate, const float *key, const float *value,
+                 const float *q_norm, const float *k_norm,
+                 int batch, int position, float epsilon,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
+/* Device-resident DeltaNet layer: the operation k_delta performs in the
+ * reference model loop (src/kernels.cu:557-566, src/runtime.cu:384-397).
+ * Same layouts as qv_test_delta; batch >= 1; asynchronous on `stream`. */
+int qv_delta(float *out, float *state, float *history,
+             const float *qkv, const float *gate,
+             const float *alpha, const float *beta,
+             const float *conv, const float *decay,
+             const float *bias, const float *norm,
+             int batch, int key_heads, int value_heads, int dim,
+             float epsilon, void *stream);
+
+/* Sequence-split decode across GPUs.  A shard cache holds the absolute
+ * positions [shard_begin, shard_begin+shard_rows) as rows [0,shard_rows).
+ * When shard_begin+shard_rows == position the batch's new rows are appended
+ * to this shard (capacity >= shard_rows+batch) and attended; otherwise the
+ * shard must lie wholly before position.  Writes the shard's normalised
+ * partial [batch,24,256] (no gate) and natural-log LSE [batch,24] (-inf for
+ * rows that see no key).  batch 1..21.  qv_attention_merge combines `shards`
+ * stacked partials [shards,batch,24,256] / LSEs [shards,batch,24] into the
+ * gated output [batch,24,256]. */
+size_t qv_attention_shard_workspace(int batch, int shard_rows);
+int qv_attention_shard(float *partial, float *lse, void *key_cache, void *value_cache,
+                       int shard_begin, int shard_rows,
+                       const float *q_gate, const float *key, const float *value,
+                       const float *q_norm, const float *k_norm,
+                       int batch, int position, float epsilon,
+                       void *workspace, size_t workspace_bytes, void *stream);
+int qv_attention_merge(float *out, const float *partials, const float *lses, int shards,
+                       int batch, const float *q_gate, void *stream);
+
+/* Core causal prefill attention (no norm, RoPE or gate), device memory:
+ * q [tokens,24,256] fp16 at absolute positions position..position+tokens-1;
+ * caches [position+tokens,4,256] fp16; out [tokens,24,256] fp32 =
+ * softmax(q.k/16 over keys <= own position) v; lse [tokens,24] natural log
+ * (may be NULL).  Asynchronous on `stream`. */
+int qv_prefill_attention(float *out, float *lse, const void *q,
+                         const void *key_cache, const void *value_cache,
+                         int tokens, int position, void *stream);
+
+/* Core gated-DeltaNet recurrence over a prefill block (no conv, no gated
+ * norm), device memory: raw q,k [tokens,key_heads,D] fp16 (L2-normalised
+ * inside; q also by 1/sqrt(D)), v [tokens,value_heads,D] fp16, alpha/beta
+ * raw [tokens,value_heads] (log decay = decay*softplus(alpha+bias), beta =
+ * sigmoid(beta)), state [value_heads,D,D] fp32 in/out; out
+ * [tokens,value_heads,D] fp32 is the state readout before the gated norm. */
+int qv_delta_core(float *out, float *state, const void *q, const void *k, const void *v,
+                  const float *alpha, const float *beta, const float *decay, const float *bias,
+                  int tokens, int key_heads, int value_heads, int dim, void *stream);
+
+/* Synchronise the current device and return (then clear) the status word
+ * that kernels set when a bounded internal wait gives up: 0 = none. */
+int qv_status(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

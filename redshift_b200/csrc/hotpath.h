@@ -1,0 +1,34 @@
+// Internal C++ launch API of the hot-path kernels (not part of the C ABI).
+// All functions are stream-ordered, take device pointers and throw
+// std::exception subclasses on invalid arguments or launch failures.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace qv {
+
+// Attention (attention.cu).  Cache layout [rows][4][256] fp16.
+size_t attention_workspace_bytes(int T, int kv_rows);
+void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const float *q_gate,
+                   const float *key, const float *value, const float *qn, const float *kn, int T,
+                   int position, int kv_begin, int kv_rows, bool append, float eps, void *ws,
+                   size_t ws_bytes, cudaStream_t st);
+void attention_merge(float *out, const float *parts, const float *lses, int shards, int T,
+                     const float *q_gate, cudaStream_t st);
+void prefill_core(float *out, float *lse, const __half *q, const __half *kc, const __half *vc, int T,
+                  int position, cudaStream_t st);
+
+// Gated DeltaNet (delta.cu).
+void delta_run(float *out, float *state, float *history, const float *qkv, const float *gate,
+               const float *alpha, const float *beta, const float *conv, const float *decay,
+               const float *bias, const float *norm, int T, int Hk, int Hv, int D, float eps,
+               cudaStream_t st);
+void delta_core_recurrent(float *out, float *state, const __half *q, const __half *k, const __half *v,
+                          const float *alpha, const float *beta, const float *decay, const float *bias,
+                          int T, int Hk, int Hv, int D, cudaStream_t st);
+
+// Device status word (status.cu): 0 = ok, else the first error a kernel raised.
+int read_and_clear_status();
+
+}  // namespace qv

@@ -1,0 +1,184 @@
+"""Parity of the CUDA path with the CPU oracle on the seeded benchmark
+configurations (0-4), through the C ABI.
+
+Tolerances: the north-star bounds (attention max-abs <= 2e-3, DeltaNet state
+relative <= 1e-3) and, where the reference defines one, its own scaled
+criterion |a-e| <= tol*(1+|e|)."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from oracle import inputs as I
+from tests.test_cuda import close, run_attention, run_delta
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / 'golden'
+ATTN_MAX_ABS = 2e-3
+DELTA_STATE_REL = 1e-3
+
+
+def rel_err(a, e):
+    a, e = np.asarray(a, np.float64), np.asarray(e, np.float64)
+    return np.abs(a - e).max() / max(np.abs(e).max(), 1e-30)
+
+
+# ------------------------------------------------------------------ config 0
+def test_config0_attention_against_reference_golden(lib):
+    c = I.attention_layer(batch=8, position=128)
+    g = np.load(GOLDEN / 'attention_cfg0.npz')
+    out, kc, vc = run_attention(lib, c, kc=c['key_cache'].copy(), vc=c['value_cache'].copy())
+    assert np.abs(out - g['out']).max() <= ATTN_MAX_ABS
+    close(out, g['out'], 3e-4)
+    close(kc[128:].reshape(-1).astype(np.float64), g['new_k'], 2e-3)
+    assert np.array_equal(vc[128:].reshape(-1).astype(np.float64), g['new_v'])
+
+
+@pytest.mark.parametrize('name', ['attention_edge', 'attention_single'])
+def test_attention_golden_edges(lib, name):
+    g = np.load(GOLDEN / f'{name}.npz')
+    c = {'attention_edge': lambda: I.attention_layer(batch=8, position=250, seed=1100),
+         'attention_single': lambda: I.attention_layer(batch=1, position=0, seed=1101)}[name]()
+    out, _, _ = run_attention(lib, c, kc=c['key_cache'].copy(), vc=c['value_cache'].copy())
+    close(out, g['out'], 3e-4)
+
+
+# ------------------------------------------------------------------ config 1
+def test_config1_delta_against_reference_golden(lib):
+    c = I.delta_layer(batch=8)
+    g = np.load(GOLDEN / 'delta_cfg1.npz')
+    out, st, hi = run_delta(lib, c)
+    close(out, g['out'])
+    st = st.reshape(48, 128, 128)[g['state_heads']]
+    assert rel_err(st, g['state']) <= DELTA_STATE_REL
+    close(st, g['state'])
+    np.testing.assert_array_equal(hi, g['history'])
+
+
+def test_config1_full_state_against_oracle(lib):
+    c = I.delta_layer(batch=8)
+    exp_out, exp_state, exp_hist = oracle.delta(**c)
+    out, st, hi = run_delta(lib, c)
+    assert rel_err(st, exp_state) <= DELTA_STATE_REL
+    close(st, exp_state)
+    close(out, exp_out)
+
+
+def test_delta_golden_small(lib):
+    g = np.load(GOLDEN / 'delta_small_t1.npz')
+    c = I.delta_layer(batch=1, seed=1102, key_heads=4, value_heads=12, dim=128, state_std=0.05)
+    out, st, _ = run_delta(lib, c)
+    close(out, g['out'])
+    close(st.reshape(12, 128, 128)[g['state_heads']], g['state'])
+
+
+# ------------------------------------------------------------------ config 2
+@pytest.mark.parametrize('context', [32768, 139264])
+def test_config2_long_context_attention(lib, context):
+    c = I.attention_layer(batch=8, position=context - 8, seed=1002)
+    exp_out, exp_k, _ = oracle.attention(**c)
+    out, kc, vc = run_attention(lib, c, kc=c['key_cache'].copy(), vc=c['value_cache'].copy())
+    assert np.abs(out - exp_out).max() <= ATTN_MAX_ABS
+    close(out, exp_out, 3e-4)
+    close(kc[-8:].astype(np.float64), exp_k[-8:].astype(np.float64), 2e-3)
+
+
+@pytest.mark.parametrize('position,batch', [(0, 8), (63, 1), (64, 8), (1000, 5), (2041, 8), (2047, 1)])
+def test_attention_tile_edges(lib, position, batch):
+    c = I.attention_layer(batch=batch, position=position, seed=2000 + position)
+    exp_out, _, _ = oracle.attention(**c)
+    out, _, _ = run_attention(lib, c, kc=c['key_cache'].copy(), vc=c['value_cache'].copy())
+    close(out, exp_out, 3e-4)
+
+
+# ------------------------------------------------------------------ prefill (ABI level)
+@pytest.mark.parametrize('position,batch', [(0, 9), (100, 21), (37, 300), (0, 1000)])
+def test_attention_prefill_abi(lib, position, batch):
+    c = I.attention_layer(batch=batch, position=position, seed=3000 + batch)
+    exp_out, exp_k, exp_v = oracle.attention(**c)
+    out, kc, vc = run_attention(lib, c, kc=c['key_cache'].copy(), vc=c['value_cache'].copy(),
+                                fn=lib.qv_test_attention_prefill)
+    assert np.abs(out - exp_out).max() <= ATTN_MAX_ABS
+    close(out, exp_out, 3e-4)
+    assert np.array_equal(vc.astype(np.float64), exp_v.astype(np.float64))
+
+
+def test_delta_prefill_abi(lib):
+    c = I.delta_layer(batch=100, seed=3100, key_heads=4, value_heads=12, dim=128, state_std=0.05)
+    exp_out, exp_state, exp_hist = oracle.delta(**c)
+    out = np.zeros(100 * 12 * 128, np.float32)
+    st, hi = c['state'].copy(), c['history'].copy()
+    f = lambda k: np.ascontiguousarray(np.asarray(c[k], np.float32).reshape(-1))  # noqa: E731
+    from tests.test_cuda import ptr
+    a = {k: f(k) for k in ('qkv', 'gate', 'alpha', 'beta', 'conv', 'decay', 'bias', 'norm')}
+    rc = lib.qv_test_delta_prefill(ptr(out), ptr(st), ptr(hi), ptr(a['qkv']), ptr(a['gate']), ptr(a['alpha']),
+                                   ptr(a['beta']), ptr(a['conv']), ptr(a['decay']), ptr(a['bias']),
+                                   ptr(a['norm']), 100, 4, 12, 128, 1e-6)
+    assert rc == 0, lib.qv_error()
+    close(out, exp_out, 1e-4)
+    assert rel_err(st, exp_state) <= DELTA_STATE_REL
+    close(hi, exp_hist, 0)
+
+
+# ------------------------------------------------------------------ config 3 (core prefill)
+def _prefill_gpu(hot, q, k, v, position=0):
+    import torch
+    L = q.shape[0]
+    dev = torch.device('cuda')
+    qt = torch.from_numpy(q.view(np.uint16).copy()).to(dev).view(torch.float16)
+    kt = torch.from_numpy(k.view(np.uint16).copy()).to(dev).view(torch.float16)
+    vt = torch.from_numpy(v.view(np.uint16).copy()).to(dev).view(torch.float16)
+    out = torch.empty((L, 24, 256), dtype=torch.float32, device=dev)
+    lse = torch.empty((L, 24), dtype=torch.float32, device=dev)
+    hot.prefill_attention(out, qt, kt, vt, L, position, lse=lse)
+    assert hot.status() == 0
+    return out.cpu().numpy(), lse.cpu().numpy()
+
+
+def test_config3_prefill_sampled_rows(hot):
+    q, k, v = I.prefill_attention(length=4096)
+    out, lse = _prefill_gpu(hot, q, k, v)
+    rng = np.random.default_rng(99)
+    rows = np.unique(np.concatenate([[0, 1, 63, 64, 127, 128, 2047, 4094, 4095], rng.integers(0, 4096, 40)]))
+    heads = [0, 5, 6, 11, 17, 23]
+    exp, exp_lse = oracle.prefill_attention_core(q, k, v, rows=rows, heads=heads)
+    got = out[rows][:, heads]
+    assert np.abs(got - exp).max() <= ATTN_MAX_ABS
+    close(got, exp, 3e-4)
+    np.testing.assert_allclose(lse[rows][:, heads], exp_lse, atol=1e-3, rtol=0)
+
+
+@pytest.mark.parametrize('L,position', [(1000, 0), (200, 77)])
+def test_prefill_core_full(hot, L, position):
+    q, k, v = I.prefill_attention(length=L + position, seed=1200 + L)
+    q = q[position:]
+    out, lse = _prefill_gpu(hot, q, k, v, position)
+    exp, exp_lse = oracle.prefill_attention_core(q, k, v, position=position)
+    close(out, exp, 3e-4)
+    np.testing.assert_allclose(lse, exp_lse, atol=1e-3, rtol=0)
+
+
+# ------------------------------------------------------------------ config 4 (core DeltaNet)
+def _delta_core_gpu(hot, c, state):
+    import torch
+    dev = torch.device('cuda')
+    L, hk, d = c['q'].shape
+    hv = c['v'].shape[1]
+    t16 = lambda a: torch.from_numpy(a.view(np.uint16).copy()).to(dev).view(torch.float16)  # noqa: E731
+    t32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)  # noqa: E731
+    st = t32(state)
+    out = torch.empty((L, hv, d), dtype=torch.float32, device=dev)
+    hot.delta_core(out, st, t16(c['q']), t16(c['k']), t16(c['v']), t32(c['alpha']), t32(c['beta']),
+                   t32(np.full(hv, -1.0)), t32(np.zeros(hv)), L, hk, hv, d)
+    assert hot.status() == 0
+    return out.cpu().numpy(), st.cpu().numpy()
+
+
+def test_config4_delta_core_against_recurrence(hot):
+    c = I.delta_prefill(length=512)
+    q, k, g, b = oracle.hotpath.prepare_delta_inputs(c['q'], c['k'], c['alpha'], c['beta'])
+    exp_out, exp_state = oracle.delta_core(np.zeros((48, 128, 128)), q, k, c['v'], g, b)
+    out, st = _delta_core_gpu(hot, c, np.zeros((48, 128, 128), np.float32))
+    assert rel_err(st, exp_state) <= DELTA_STATE_REL
+    close(out, exp_out, 1e-4)
