@@ -127,7 +127,7 @@ int qv_delta(float *out, float *state, float *history,
  * to this shard (capacity >= shard_rows+batch) and attended; otherwise the
  * shard must lie wholly before position.  Writes the shard's normalised
  * partial [batch,24,256] (no gate) and natural-log LSE [batch,24] (-inf for
- * rows that see no key).  batch 1..21.  qv_attention_merge combines `shards`
+ * rows that see no key).  batch 1..10.  qv_attention_merge combines `shards`
  * stacked partials [shards,batch,24,256] / LSEs [shards,batch,24] into the
  * gated output [batch,24,256]. */
 size_t qv_attention_shard_workspace(int batch, int shard_rows);

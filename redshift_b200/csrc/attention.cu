@@ -1,13 +1,25 @@
 // Full-attention hot path for sm_100a: prepare (RMSNorm + partial RoPE + fp16
 // KV append), a tcgen05/TMEM FlashAttention kernel that serves both the
 // decode/verify regime (split-KV, all 6 GQA heads x T tokens of one KV head
-// share every K/V tile) and causal prefill (128 query positions of one head
-// per CTA), and the split/shard combine kernels.
+// share every K/V tile) and causal prefill (a tile of query positions of one
+// head per CTA), and the split/shard combine kernels.
 //
 // Semantics follow the reference's attn_prepare / attention / attention_tiled
 // (src/kernels.cu:415-503) and the CPU oracle tests/cpu_reference.py:55-89:
 // scores q.k/16 over cache rows [0, position+t], softmax, P.V, times
 // sigmoid(gate).
+//
+// Two precision modes of the FlashAttention kernel:
+//  * PRECISE (decode / verify and reference-semantics prefill): 64 query rows
+//    per CTA.  Q is split into fp16 hi = fp16(q) and lo = fp16(q - hi) and the
+//    QK MMA's A operand (held in TMEM) interleaves them: A row 32w+i = Q_hi and
+//    32w+16+i = Q_lo of query row 16w+i, so one M=128 MMA leaves both score
+//    halves of a row in lanes i and i+16 of warp w, which add them while they
+//    split the row's columns.  Every probability p is split the same way; the
+//    PV MMA's A rows 32w+i / 32w+16+i are P_hi / P_lo of row 16w+i, so O_hi and
+//    O_lo land in the same warp and are summed in the epilogue.  Scores and
+//    probabilities keep ~22 mantissa bits (the reference computes them in fp32).
+//  * FAST (core prefill, benchmark configuration 3): M=128 query rows and fp16 P.
 #include "common.cuh"
 #include "hotpath.h"
 
@@ -19,28 +31,32 @@
 namespace qv {
 
 constexpr int NQ = 24, NKV = 4, HD = 256, GROUP = NQ / NKV;
-constexpr int BM = 128;          // rows per CTA (TMEM lanes)
 constexpr int BN = 64;           // cache positions per K/V tile
-constexpr int STAGES = 2;        // K/V tile pipeline depth
+constexpr int TILE_BYTES = 4 * BN * 128;                      // one K or V tile, 4 boxes of 64 rows x 128 B
+constexpr int DECODE_ROWS = 64;                               // logical rows of a decode CTA
 constexpr float SCORE_LOG2 = 0.0625f * 1.4426950408889634f;   // (1/16) * log2(e)
 constexpr float RESCALE_THRESHOLD = 8.f;                      // lazy O rescale, log2 units
 
-// Shared-memory map of fa_kernel (offsets from a 1024-byte aligned base).
-constexpr int SM_Q = 0;                                   // 4 x [128 rows][64 d] fp16, 16 KB each
-constexpr int SM_KV = SM_Q + 4 * BM * 128;                 // per stage: K 4 x 8 KB, V 4 x 8 KB
-constexpr int SM_KV_STAGE = 2 * 4 * BN * 128;
-constexpr int SM_P = SM_KV + STAGES * SM_KV_STAGE;         // 2 x [128 rows][64 pos] fp16
-constexpr int SM_BAR = SM_P + 2 * BM * 128;
-constexpr int SM_TOTAL = SM_BAR + 256;
-constexpr int SMEM_BYTES = SM_TOTAL + 1024;                // slack for manual alignment
+constexpr int STAGES3 = 3;       // K/V tile ring depth
+template <bool PRECISE> struct FaLayout {
+    static constexpr int QROWS = PRECISE ? 64 : 128;          // logical query rows per CTA
+    static constexpr int SM_KV = 0;                           // ring of (K tile, V tile)
+    static constexpr int SM_KV_STAGE = 2 * TILE_BYTES;
+    static constexpr int SM_P = SM_KV + STAGES3 * SM_KV_STAGE; // 2 x [128 A-rows][64 pos] fp16
+    static constexpr int SM_BAR = SM_P + 2 * 128 * 128;
+    static constexpr int SMEM_BYTES = SM_BAR + 256 + 1024;    // + slack for manual alignment
+};
+// TMEM columns: S double buffer [0,128), O [128,384), Q (A operand) [384,512).
+constexpr uint32_t TM_S = 0, TM_O = 128, TM_Q = 384;
 
 struct FaParams {
-    const __half *q;        // prepared queries [T][24][256]
+    const __half *q;        // prepared queries [T][24][256] (fp16 of q)
+    const __half *q_lo;     // fp16 of (q - fp16(q)) (PRECISE)
     const float *q_gate;    // [T][24][512], gate = [256:512) (direct mode), may be null
     float *out;             // [T][24][256] (direct mode)
     float *lse;             // optional natural-log LSE [T][24] (direct mode)
-    float *part_o;          // [4][splits][128][256] unnormalised partial O (split mode)
-    float *part_ml;         // [4][splits][128][2]  (running max in log2 units, sum)
+    float *part_o;          // [4][splits][64][256] unnormalised partial O (split mode)
+    float *part_ml;         // [4][splits][64][2]  (running max in log2 units, sum)
     int T, position;        // tokens and absolute position of token 0
     int kv_begin;           // absolute position of cache row 0
     int kv_rows;            // valid cache rows
@@ -49,22 +65,40 @@ struct FaParams {
     int direct;             // 1: write final output; 0: write split partials
 };
 
-__device__ __forceinline__ void row_token_head(const FaParams &p, int r, int &t, int &h) {
-    if (p.mode == 0) { t = r / GROUP; h = blockIdx.y * GROUP + r % GROUP; }
-    else { t = (gridDim.y - 1 - blockIdx.y) * BM + r; h = blockIdx.x; }
+// Logical query row -> (token, head).  Decode packs the 6 heads of one KV head
+// and the T tokens; prefill takes QROWS consecutive tokens of one head.
+template <int QROWS>
+__device__ __forceinline__ bool row_token_head(const FaParams &p, int r, int &t, int &h) {
+    if (p.mode == 0) {
+        t = r / GROUP;
+        h = blockIdx.y * GROUP + r % GROUP;
+        return r < p.T * GROUP;
+    }
+    t = (gridDim.y - 1 - blockIdx.y) * QROWS + r;
+    h = blockIdx.x;
+    return t < p.T;
 }
 
+// Warp-uniform bounded wait (all lanes agree on the outcome).
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+}
+
+template <bool PRECISE>
 __global__ void __launch_bounds__(256, 1)
 fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
           const FaParams p) {
+    using L = FaLayout<PRECISE>;
+    constexpr int QROWS = L::QROWS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SM_BAR);
-    uint64_t *k_full = bars, *v_full = bars + 2, *kv_empty = bars + 4, *s_full = bars + 6,
-             *s_free = bars + 8, *p_full = bars + 10, *p_free = bars + 12, *mma_done = bars + 14;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SM_BAR + 128);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + SM_BAR + 132);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::SM_BAR);
+    uint64_t *k_full = bars, *v_full = bars + 3, *k_empty = bars + 6, *v_empty = bars + 9,
+             *s_full = bars + 12, *s_free = bars + 14, *p_full = bars + 16, *p_free = bars + 18,
+             *mma_done = bars + 20;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::SM_BAR + 192);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::SM_BAR + 196);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kv_head = p.mode == 0 ? blockIdx.y : blockIdx.x / GROUP;
@@ -77,15 +111,18 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         ntiles = min(p.split_tiles, total - tile0);
     } else {
         const int qtile = gridDim.y - 1 - blockIdx.y;
-        const int last_tok = min(p.T, (qtile + 1) * BM) - 1;
+        const int last_tok = min(p.T, (qtile + 1) * QROWS) - 1;
         const int limit = min(p.kv_rows, p.position + last_tok - p.kv_begin + 1);
         tile0 = 0;
         ntiles = (limit + BN - 1) / BN;
     }
 
     if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES3; ++i) {
+            mbar_init(k_full + i, 1); mbar_init(v_full + i, 1);
+            mbar_init(k_empty + i, 1); mbar_init(v_empty + i, 1);
+        }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(k_full + i, 1); mbar_init(v_full + i, 1); mbar_init(kv_empty + i, 1);
             mbar_init(s_full + i, 1); mbar_init(s_free + i, 4);
             mbar_init(p_full + i, 4); mbar_init(p_free + i, 1);
         }
@@ -95,81 +132,99 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     }
     if (warp == 0 && lane == 0) { prefetch_tmap(&tmK); prefetch_tmap(&tmV); }
     if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
-
-    // Stage the query rows into the 128B-swizzled K-major layout of operand A.
-    // Rows without a (token, head) are zero.
-    for (int u = threadIdx.x; u < BM * 32; u += blockDim.x) {
-        const int r = u >> 5, unit = u & 31, chunk = unit >> 3, w = unit & 7;
-        int t, h;
-        row_token_head(p, r, t, h);
-        const bool valid = (p.mode == 0 ? r < p.T * GROUP : true) && t < p.T;
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (valid) val = *reinterpret_cast<const uint4 *>(p.q + ((size_t)t * NQ + h) * HD + unit * 8);
-        *reinterpret_cast<uint4 *>(smem + SM_Q + chunk * (BM * 128) + r * 128 + ((w ^ (r & 7)) << 4)) = val;
-    }
-    fence_async_shared();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Softmax warps 4-7: thread = TMEM lane = A row of the QK MMA.
+    // FAST: A row = query row.  PRECISE: lanes i and i+16 of warp w carry the
+    // hi and lo halves of query row 16w+i (one M=128 MMA yields both).
+    const int wq = warp - 4;
+    const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const int half = PRECISE ? (lane >> 4) : 0;
+    const int r = PRECISE ? wq * 16 + (lane & 15) : wq * 32 + lane;     // logical query row
+    int t = 0, h = 0;
+    const bool valid = warp >= 4 && row_token_head<QROWS>(p, r, t, h);
+    if (warp >= 4) {
+        // Stage this lane's query row (256 fp16 = 128 columns) into TMEM.
+        const __half *src = (PRECISE && half) ? p.q_lo : p.q;
+        const uint4 *row = reinterpret_cast<const uint4 *>(src + ((size_t)t * NQ + h) * HD);
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+            uint4 u[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) u[e] = valid ? row[c * 4 + e] : make_uint4(0, 0, 0, 0);
+            tmem_st16(t_lane + TM_Q + c * 16, *reinterpret_cast<const float(*)[16]>(u));
+        }
+        tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
+        // K tiles are released after QK, V tiles after PV, so the next K load
+        // overlaps the softmax and PV of the current tile.
         if (lane == 0) {
-            int issued = 0;
+            int k_issued = 0, v_issued = 0;
             for (int j = 0; j < ntiles; ++j) {
-                const int s = j & 1;
-                if (j >= STAGES && !mbar_wait(kv_empty + s, ((j >> 1) - 1) & 1, abort_flag)) break;
+                const int s = j % STAGES3;
+                const uint32_t use = (uint32_t)(j / STAGES3);
                 const int y = (tile0 + j) * BN;
-                uint8_t *kd = smem + SM_KV + s * SM_KV_STAGE, *vd = kd + 4 * BN * 128;
-                mbar_expect_tx(k_full + s, 4 * BN * 128);
+                uint8_t *kd = smem + L::SM_KV + s * L::SM_KV_STAGE, *vd = kd + TILE_BYTES;
+                if (j >= STAGES3 && !mbar_wait(k_empty + s, (use - 1) & 1, abort_flag)) break;
+                mbar_expect_tx(k_full + s, TILE_BYTES);
                 for (int c = 0; c < 4; ++c) tma_load_2d(kd + c * BN * 128, &tmK, k_full + s, kv_head * HD + c * 64, y);
-                mbar_expect_tx(v_full + s, 4 * BN * 128);
+                k_issued = j + 1;
+                if (j >= STAGES3 && !mbar_wait(v_empty + s, (use - 1) & 1, abort_flag)) break;
+                mbar_expect_tx(v_full + s, TILE_BYTES);
                 for (int c = 0; c < 4; ++c) tma_load_2d(vd + c * BN * 128, &tmV, v_full + s, kv_head * HD + c * 64, y);
-                issued = j + 1;
+                v_issued = j + 1;
             }
             // Drain: every issued load must land before the CTA may exit.
-            for (int j = max(0, issued - 2); j < issued; ++j) {
-                const long long t0 = clock64();
-                while (!mbar_try_wait(v_full + (j & 1), (j >> 1) & 1) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
-                while (!mbar_try_wait(k_full + (j & 1), (j >> 1) & 1) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
-            }
+            const long long t0 = clock64();
+            for (int j = max(0, k_issued - STAGES3); j < k_issued; ++j)
+                while (!mbar_try_wait(k_full + j % STAGES3, (j / STAGES3) & 1) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
+            for (int j = max(0, v_issued - STAGES3); j < v_issued; ++j)
+                while (!mbar_try_wait(v_full + j % STAGES3, (j / STAGES3) & 1) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc_qk = idesc_f16(BM, BN, false, false);
-            const uint32_t idesc_pv = idesc_f16(BM, HD, false, true);
-            const uint32_t q_base = smem_addr(smem + SM_Q);
+            const uint32_t idesc_qk = idesc_f16(128, BN, false, false);
+            const uint32_t idesc_pv = idesc_f16(128, HD, false, true);
             auto issue_pv = [&](int i) -> bool {
-                const int s = i & 1;
-                if (!mbar_wait(p_full + s, (i >> 1) & 1, abort_flag)) return false;
-                if (!mbar_wait(v_full + s, (i >> 1) & 1, abort_flag)) return false;
+                const int b = i & 1, s = i % STAGES3;
+                if (!mbar_wait(p_full + b, (i >> 1) & 1, abort_flag)) return false;
+                if (!mbar_wait(v_full + s, (i / STAGES3) & 1, abort_flag)) return false;
                 tc_fence_after();
-                const uint32_t pa = smem_addr(smem + SM_P + s * BM * 128);
-                const uint32_t vb = smem_addr(smem + SM_KV + s * SM_KV_STAGE + 4 * BN * 128);
+                const uint32_t pa = smem_addr(smem + L::SM_P + b * 128 * 128);
+                const uint32_t vb = smem_addr(smem + L::SM_KV + s * L::SM_KV_STAGE + TILE_BYTES);
 #pragma unroll
                 for (int k = 0; k < BN / 16; ++k)
-                    mma_f16_ss(tmem + 128, sw128_desc(pa + k * 32, 16, 1024),
+                    mma_f16_ss(tmem + TM_O, sw128_desc(pa + k * 32, 16, 1024),
                                sw128_desc(vb + k * 16 * 128, BN * 128, 1024), idesc_pv,
                                (i > 0 || k > 0) ? 1u : 0u);
-                mma_commit(p_free + s);
-                mma_commit(kv_empty + s);
+                mma_commit(p_free + b);
+                mma_commit(v_empty + s);
                 return true;
             };
             bool ok = true;
             for (int j = 0; j < ntiles && ok; ++j) {
-                const int s = j & 1;
-                if (!mbar_wait(k_full + s, (j >> 1) & 1, abort_flag)) { ok = false; break; }
-                if (j >= 2 && !mbar_wait(s_free + s, ((j >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
+                const int b = j & 1, s = j % STAGES3;
+                if (!mbar_wait(k_full + s, (j / STAGES3) & 1, abort_flag)) { ok = false; break; }
+                if (j >= 2 && !mbar_wait(s_free + b, ((j >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t kb = smem_addr(smem + SM_KV + s * SM_KV_STAGE);
+                const uint32_t kb = smem_addr(smem + L::SM_KV + s * L::SM_KV_STAGE);
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k)
-                    mma_f16_ss(tmem + s * BN, sw128_desc(q_base + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024),
+                    mma_f16_ts(tmem + TM_S + b * BN, tmem + TM_Q + k * 8,
                                sw128_desc(kb + (k >> 2) * (BN * 128) + (k & 3) * 32, 16, 1024),
                                idesc_qk, k > 0 ? 1u : 0u);
-                mma_commit(s_full + s);
+                mma_commit(s_full + b);
+                mma_commit(k_empty + s);
                 if (j >= 1) ok = issue_pv(j - 1);
             }
             if (ok && ntiles > 0) issue_pv(ntiles - 1);
@@ -180,115 +235,142 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         }
     } else if (warp >= 4) {
         // ------------------------------------------------ softmax + epilogue
-        const int wq = warp - 4, r = wq * 32 + lane;
-        const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
-        int t, h;
-        row_token_head(p, r, t, h);
-        const bool valid = (p.mode == 0 ? r < p.T * GROUP : true) && t < p.T;
+        // FAST: each thread owns a query row and all 64 columns of a tile.
+        // PRECISE: lane i keeps columns [0,32) and lane i+16 columns [32,64) of
+        // row 16w+i, each summing the hi and lo score halves, and each writes
+        // the hi and lo probabilities of its columns.
+        constexpr int NC = PRECISE ? 32 : 64;                      // columns per thread
         const int pos_limit = valid ? p.position + t - p.kv_begin : -1;   // last visible local row
+        const int arow_hi = PRECISE ? wq * 32 + (lane & 15) : r;         // A rows of P (hi, lo)
+        const int arow_lo = arow_hi + 16;
         float m_use = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < ntiles; ++j) {
-            const int s = j & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(s_full + s, (j >> 1) & 1, abort_flag))) { ok = false; break; }
+            const int b = j & 1;
+            if (!warp_wait(s_full + b, (j >> 1) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            float x[BN];
+            float x[64];
 #pragma unroll
-            for (int c = 0; c < BN / 16; ++c) tmem_ld16(t_lane + s * BN + c * 16, *reinterpret_cast<float(*)[16]>(x + c * 16));
+            for (int c = 0; c < 4; ++c) tmem_ld16(t_lane + TM_S + b * BN + c * 16, *reinterpret_cast<float(*)[16]>(x + c * 16));
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(s_free + s);
-            const int key0 = (tile0 + j) * BN;
+            if (lane == 0) mbar_arrive(s_free + b);
+            if (PRECISE) {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const float recv = __shfl_xor_sync(0xffffffffu, half ? x[c] : x[32 + c], 16);
+                    x[c] = (half ? x[32 + c] : x[c]) + recv;
+                }
+            }
+            const int key0 = (tile0 + j) * BN + half * 32;
             const int lim = min(pos_limit, p.kv_rows - 1) - key0;     // columns <= lim are visible
             float m_tile = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
+            for (int c = 0; c < NC; ++c) {
                 x[c] = c <= lim ? x[c] * SCORE_LOG2 : -INFINITY;
                 m_tile = fmaxf(m_tile, x[c]);
             }
+            if (PRECISE) m_tile = fmaxf(m_tile, __shfl_xor_sync(0xffffffffu, m_tile, 16));
             float factor = 1.f;
             const bool need = m_tile > m_use + RESCALE_THRESHOLD;
             if (need) { factor = exp2f(m_use - m_tile); m_use = m_tile; l *= factor; }
             if (j > 0 && __any_sync(0xffffffffu, need)) {
                 // O already holds tiles < j: wait for PV(j-1), then rescale rows in TMEM.
-                if (!__all_sync(0xffffffffu, mbar_wait(p_free + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag))) { ok = false; break; }
+                if (!warp_wait(p_free + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll 1
                 for (int c = 0; c < HD / 16; ++c) {
                     float o[16];
-                    tmem_ld16(t_lane + 128 + c * 16, o);
+                    tmem_ld16(t_lane + TM_O + c * 16, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 16; ++e) o[e] *= factor;
-                    tmem_st16(t_lane + 128 + c * 16, o);
+                    tmem_st16(t_lane + TM_O + c * 16, o);
                 }
                 tmem_wait_st();
             }
             const float mref = m_use == -INFINITY ? 0.f : m_use;
-            uint32_t packed[BN / 2];
+            uint32_t hi[NC / 2], lo[PRECISE ? NC / 2 : 1];
             float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < BN; c += 2) {
-                const __half2 hp = __floats2half2_rn(exp2f(x[c] - mref), exp2f(x[c + 1] - mref));
+            for (int c = 0; c < NC; c += 2) {
+                const float p0 = exp2f(x[c] - mref), p1 = exp2f(x[c + 1] - mref);
+                const __half2 hp = __floats2half2_rn(p0, p1);
+                hi[c / 2] = *reinterpret_cast<const uint32_t *>(&hp);
                 const float2 back = __half22float2(hp);
-                sum += back.x + back.y;
-                packed[c / 2] = *reinterpret_cast<const uint32_t *>(&hp);
+                if (PRECISE) {
+                    const __half2 lp = __floats2half2_rn(p0 - back.x, p1 - back.y);
+                    lo[c / 2] = *reinterpret_cast<const uint32_t *>(&lp);
+                    sum += p0 + p1;
+                } else {
+                    sum += back.x + back.y;
+                }
             }
             l += sum;
-            if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(p_free + s, ((j - 2) >> 1) & 1, abort_flag))) { ok = false; break; }
-            uint8_t *prow = smem + SM_P + s * BM * 128 + r * 128;
+            if (j >= 2 && !warp_wait(p_free + b, ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
+            uint8_t *pbuf = smem + L::SM_P + b * 128 * 128;
+            if (PRECISE) {
 #pragma unroll
-            for (int w = 0; w < 8; ++w)
-                *reinterpret_cast<uint4 *>(prow + ((w ^ (r & 7)) << 4)) =
-                    make_uint4(packed[4 * w], packed[4 * w + 1], packed[4 * w + 2], packed[4 * w + 3]);
+                for (int w = 0; w < 4; ++w) {
+                    const int unit = half * 4 + w;
+                    *reinterpret_cast<uint4 *>(pbuf + arow_hi * 128 + ((unit ^ (arow_hi & 7)) << 4)) =
+                        make_uint4(hi[4 * w], hi[4 * w + 1], hi[4 * w + 2], hi[4 * w + 3]);
+                    *reinterpret_cast<uint4 *>(pbuf + arow_lo * 128 + ((unit ^ (arow_lo & 7)) << 4)) =
+                        make_uint4(lo[4 * w], lo[4 * w + 1], lo[4 * w + 2], lo[4 * w + 3]);
+                }
+            } else {
+#pragma unroll
+                for (int w = 0; w < 8; ++w)
+                    *reinterpret_cast<uint4 *>(pbuf + arow_hi * 128 + ((w ^ (arow_hi & 7)) << 4)) =
+                        make_uint4(hi[4 * w], hi[4 * w + 1], hi[4 * w + 2], hi[4 * w + 3]);
+            }
             fence_async_shared();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full + s);
+            if (lane == 0) mbar_arrive(p_full + b);
         }
+        if (PRECISE) l += __shfl_xor_sync(0xffffffffu, l, 16);
         // Epilogue: the final PV's commit on p_free marks O complete.
-        if (ok && ntiles > 0 &&
-            __all_sync(0xffffffffu, mbar_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag))) {
+        if (ok && ntiles > 0 && warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag)) {
             tc_fence_after();
+            const bool writer = valid && (!PRECISE || half == 0);
+            float *dst;
+            const float *gate = nullptr;
+            float inv = 1.f;
             if (p.direct) {
-                const float inv = valid && l > 0.f ? 1.f / l : 0.f;
-                float *dst = valid ? p.out + ((size_t)t * NQ + h) * HD : nullptr;
-                const float *gate = valid && p.q_gate ? p.q_gate + ((size_t)t * NQ + h) * 2 * HD + HD : nullptr;
+                inv = l > 0.f ? 1.f / l : 0.f;
+                dst = writer ? p.out + ((size_t)t * NQ + h) * HD : nullptr;
+                gate = writer && p.q_gate ? p.q_gate + ((size_t)t * NQ + h) * 2 * HD + HD : nullptr;
+            } else {
+                const size_t slot = ((size_t)kv_head * p.splits + blockIdx.x) * DECODE_ROWS + r;
+                dst = writer ? p.part_o + slot * HD : nullptr;
+                if (writer) { p.part_ml[slot * 2] = m_use; p.part_ml[slot * 2 + 1] = l; }
+            }
 #pragma unroll 1
-                for (int c = 0; c < HD / 16; ++c) {
-                    float o[16];
-                    tmem_ld16(t_lane + 128 + c * 16, o);
-                    tmem_wait_ld();
-                    if (dst) {
+            for (int c = 0; c < HD / 16; ++c) {
+                float o[16];
+                tmem_ld16(t_lane + TM_O + c * 16, o);
+                tmem_wait_ld();
+                if (PRECISE) {
 #pragma unroll
-                        for (int e = 0; e < 16; e += 4) {
-                            float4 v = make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
-                            if (gate) {
-                                const float4 g = *reinterpret_cast<const float4 *>(gate + c * 16 + e);
-                                v.x *= sigmoidf_(g.x); v.y *= sigmoidf_(g.y);
-                                v.z *= sigmoidf_(g.z); v.w *= sigmoidf_(g.w);
-                            }
-                            *reinterpret_cast<float4 *>(dst + c * 16 + e) = v;
+                    for (int e = 0; e < 16; ++e) o[e] += __shfl_down_sync(0xffffffffu, o[e], 16);
+                }
+                if (dst) {
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4) {
+                        float4 v = make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
+                        if (gate) {
+                            const float4 g = *reinterpret_cast<const float4 *>(gate + c * 16 + e);
+                            v.x *= sigmoidf_(g.x); v.y *= sigmoidf_(g.y);
+                            v.z *= sigmoidf_(g.z); v.w *= sigmoidf_(g.w);
                         }
+                        *reinterpret_cast<float4 *>(dst + c * 16 + e) = v;
                     }
                 }
-                if (valid && p.lse) p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * 0.6931471805599453f : -INFINITY;
-            } else {
-                const size_t slot = ((size_t)kv_head * p.splits + blockIdx.x) * BM + r;
-                float *dst = p.part_o + slot * HD;
-#pragma unroll 1
-                for (int c = 0; c < HD / 16; ++c) {
-                    float o[16];
-                    tmem_ld16(t_lane + 128 + c * 16, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4 *>(dst + c * 16 + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
-                }
-                p.part_ml[slot * 2] = m_use;
-                p.part_ml[slot * 2 + 1] = l;
             }
+            if (p.direct && writer && p.lse)
+                p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * 0.6931471805599453f : -INFINITY;
         }
     }
     tc_fence_before();
@@ -304,7 +386,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
 // as fp16 operand rows, keys/values rounded to fp16 into the cache.
 __global__ void __launch_bounds__(256)
 attn_prepare_kernel(const float *q_gate, const float *key, const float *value, const float *qn,
-                    const float *kn, __half *qw, __half *kc, __half *vc, int position,
+                    const float *kn, __half *qw, __half *qw_lo, __half *kc, __half *vc, int position,
                     int append_row0, float eps) {
     const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
     const bool isq = h < NQ;
@@ -331,7 +413,9 @@ attn_prepare_kernel(const float *q_gate, const float *key, const float *value, c
     }
     __syncthreads();
     if (isq) {
-        qw[((size_t)t * NQ + h) * HD + i] = __float2half_rn(row[i]);
+        const __half hi = __float2half_rn(row[i]);
+        qw[((size_t)t * NQ + h) * HD + i] = hi;
+        if (qw_lo) qw_lo[((size_t)t * NQ + h) * HD + i] = __float2half_rn(row[i] - __half2float(hi));
     } else if (append_row0 >= 0) {
         const size_t o = ((size_t)(append_row0 + t) * NKV + kh) * HD + i;
         kc[o] = __float2half_rn(row[i]);
@@ -340,26 +424,49 @@ attn_prepare_kernel(const float *q_gate, const float *key, const float *value, c
 }
 
 // ---------------------------------------------------------------- combine
-// Merge the split partials of one (token, head) row.  mode_out 0: final
-// gated output; 1: normalised shard partial + natural-log LSE.
+// Merge the split partials of one (token, head) row: weights from the
+// per-split (max, sum) are formed once in shared memory, then each thread
+// (one output dimension) streams the splits with 8 independent loads in
+// flight.  final_gate 1: gated output; 0: normalised partial + natural-log LSE.
+constexpr int MAX_SPLITS = 64;
 __global__ void __launch_bounds__(256)
 attn_combine_kernel(float *out, float *out_lse, const float *part_o, const float *part_ml,
                     const float *q_gate, int splits, int final_gate) {
     const int t = blockIdx.x / NQ, h = blockIdx.x % NQ, d = threadIdx.x;
     const int g = h / GROUP, r = t * GROUP + h % GROUP;
-    float M = -INFINITY;
-    for (int s = 0; s < splits; ++s) M = fmaxf(M, part_ml[(((size_t)g * splits + s) * BM + r) * 2]);
-    float num = 0.f, den = 0.f;
-    if (M != -INFINITY) {
-        for (int s = 0; s < splits; ++s) {
-            const size_t slot = ((size_t)g * splits + s) * BM + r;
-            const float m = part_ml[slot * 2];
-            if (m == -INFINITY) continue;
-            const float w = exp2f(m - M);
-            den += w * part_ml[slot * 2 + 1];
-            num += w * part_o[slot * HD + d];
-        }
+    __shared__ float wgt[MAX_SPLITS], red[2], den_s;
+    const size_t slot0 = (size_t)g * splits * DECODE_ROWS + r;     // slot(s) = slot0 + s*DECODE_ROWS
+    float m = -INFINITY, l = 0.f;
+    if (d < splits) {
+        const float2 ml = *reinterpret_cast<const float2 *>(part_ml + (slot0 + (size_t)d * DECODE_ROWS) * 2);
+        m = ml.x; l = ml.y;
     }
+    float M = m;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (d < 64 && (d & 31) == 0) red[d >> 5] = M;
+    __syncthreads();
+    M = fmaxf(red[0], red[1]);
+    const float w = (d < splits && m != -INFINITY) ? exp2f(m - M) : 0.f;
+    if (d < MAX_SPLITS) wgt[d] = w;
+    float den = w * l;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    __syncthreads();
+    if (d < 64 && (d & 31) == 0) red[d >> 5] = den;
+    __syncthreads();
+    if (d == 0) den_s = red[0] + red[1];
+    __syncthreads();
+    den = den_s;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const float *src = part_o + slot0 * HD + d;
+    int s = 0;
+    for (; s + 8 <= splits; s += 8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += wgt[s + e] * src[(size_t)(s + e) * DECODE_ROWS * HD];
+    }
+    for (; s < splits; ++s) acc[0] += wgt[s] * src[(size_t)s * DECODE_ROWS * HD];
+    const float num = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
     const size_t o = ((size_t)t * NQ + h) * HD + d;
     if (final_gate) {
         out[o] = (den > 0.f ? num / den : 0.f) * sigmoidf_(q_gate[((size_t)t * NQ + h) * 2 * HD + HD + d]);
@@ -428,7 +535,10 @@ void check_launch(const char *what) {
 bool configured = false;
 void configure() {
     if (configured) return;
-    if (cudaFuncSetAttribute(fa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(fa_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             FaLayout<true>::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(fa_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             FaLayout<false>::SMEM_BYTES) != cudaSuccess)
         throw std::runtime_error("cannot reserve shared memory for the attention kernel");
     configured = true;
 }
@@ -439,23 +549,34 @@ struct Split { int tiles, splits; };
 Split decode_split(int kv_rows) {
     const int total = (kv_rows + BN - 1) / BN;
     const int per = (total + 36) / 37;
+    static_assert(37 <= MAX_SPLITS, "combine kernel handles up to MAX_SPLITS splits");
     return {per, (total + per - 1) / per};
 }
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+bool decode_regime(int T) { return T * GROUP <= DECODE_ROWS; }
+
+template <bool PRECISE>
+void launch_fa(const CUtensorMap &mk, const CUtensorMap &mv, const FaParams &p, dim3 grid, cudaStream_t st) {
+    fa_kernel<PRECISE><<<grid, 256, FaLayout<PRECISE>::SMEM_BYTES, st>>>(mk, mv, p);
+}
 }  // namespace
 
 size_t attention_workspace_bytes(int T, int kv_rows) {
-    size_t q = align256((size_t)T * NQ * HD * sizeof(__half));
-    if (T * GROUP > BM) return q;                        // prefill regime: direct output
+    size_t q = 2 * align256((size_t)T * NQ * HD * sizeof(__half));     // Q hi and lo
+    if (!decode_regime(T)) return q;                     // prefill regime: direct output
     const Split sp = decode_split(kv_rows);
-    return q + align256((size_t)NKV * sp.splits * BM * HD * sizeof(float)) +
-           align256((size_t)NKV * sp.splits * BM * 2 * sizeof(float));
+    return q + align256((size_t)NKV * sp.splits * DECODE_ROWS * HD * sizeof(float)) +
+           align256((size_t)NKV * sp.splits * DECODE_ROWS * 2 * sizeof(float));
 }
 
-// Core of one attention layer over a device cache holding absolute positions
+int attention_max_shard_batch() { return DECODE_ROWS / GROUP; }
+
+// One attention layer over a device cache holding absolute positions
 // [kv_begin, kv_begin + kv_rows).  New rows are appended at local row
 // position - kv_begin when append is true.  Writes either the final gated
-// output (shard_out == nullptr) or a normalised partial + LSE (shard mode).
+// output (shard_lse == nullptr) or a normalised partial + LSE (shard mode).
+// Decode / verify batches (T <= 10) use the split-KV regime; longer blocks
+// use the prefill regime with 64 query rows per CTA; both are PRECISE.
 void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const float *q_gate,
                    const float *key, const float *value, const float *qn, const float *kn, int T,
                    int position, int kv_begin, int kv_rows, bool append, float eps, void *ws,
@@ -463,21 +584,22 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
     if (ws_bytes < attention_workspace_bytes(T, kv_rows)) throw std::invalid_argument("attention workspace too small");
     configure();
     uint8_t *w = static_cast<uint8_t *>(ws);
-    __half *qw = reinterpret_cast<__half *>(w);
-    attn_prepare_kernel<<<dim3(T, NQ + NKV), 256, 0, st>>>(q_gate, key, value, qn, kn, qw, kc, vc, position,
-                                                           append ? position - kv_begin : -1, eps);
+    const size_t q_bytes = align256((size_t)T * NQ * HD * sizeof(__half));
+    __half *qw = reinterpret_cast<__half *>(w), *qw_lo = reinterpret_cast<__half *>(w + q_bytes);
+    attn_prepare_kernel<<<dim3(T, NQ + NKV), 256, 0, st>>>(q_gate, key, value, qn, kn, qw, qw_lo, kc, vc,
+                                                           position, append ? position - kv_begin : -1, eps);
     check_launch("attention prepare");
     const CUtensorMap mk = cache_map(kc, kv_rows), mv = cache_map(vc, kv_rows);
     FaParams p{};
-    p.q = qw; p.q_gate = q_gate; p.T = T; p.position = position;
+    p.q = qw; p.q_lo = qw_lo; p.q_gate = q_gate; p.T = T; p.position = position;
     p.kv_begin = kv_begin; p.kv_rows = kv_rows;
-    if (T * GROUP <= BM) {
+    if (decode_regime(T)) {
         const Split sp = decode_split(kv_rows);
         p.mode = 0; p.split_tiles = sp.tiles; p.splits = sp.splits; p.direct = 0;
-        p.part_o = reinterpret_cast<float *>(w + align256((size_t)T * NQ * HD * sizeof(__half)));
+        p.part_o = reinterpret_cast<float *>(w + 2 * q_bytes);
         p.part_ml = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(p.part_o) +
-                                              align256((size_t)NKV * sp.splits * BM * HD * sizeof(float)));
-        fa_kernel<<<dim3(sp.splits, NKV), 256, SMEM_BYTES, st>>>(mk, mv, p);
+                                              align256((size_t)NKV * sp.splits * DECODE_ROWS * HD * sizeof(float)));
+        launch_fa<true>(mk, mv, p, dim3(sp.splits, NKV), st);
         check_launch("attention decode");
         attn_combine_kernel<<<T * NQ, 256, 0, st>>>(out, shard_lse, p.part_o, p.part_ml, q_gate, sp.splits,
                                                     shard_lse ? 0 : 1);
@@ -485,7 +607,8 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
     } else {
         if (shard_lse) throw std::invalid_argument("shard partials are limited to decode batches");
         p.mode = 1; p.direct = 1; p.out = out; p.splits = 1;
-        fa_kernel<<<dim3(NQ, (T + BM - 1) / BM), 256, SMEM_BYTES, st>>>(mk, mv, p);
+        constexpr int R = FaLayout<true>::QROWS;
+        launch_fa<true>(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
         check_launch("attention prefill");
     }
 }
@@ -498,6 +621,7 @@ void attention_merge(float *out, const float *parts, const float *lses, int shar
 
 // Core-level causal prefill on already-prepared fp16 queries (no norm, RoPE
 // or gate): out [T][24][256] = softmax(q.k/16, causal) v, optional LSE.
+// FAST mode: 128 query rows per CTA, fp16 probabilities.
 void prefill_core(float *out, float *lse, const __half *q, const __half *kc, const __half *vc, int T,
                   int position, cudaStream_t st) {
     configure();
@@ -506,7 +630,8 @@ void prefill_core(float *out, float *lse, const __half *q, const __half *kc, con
     FaParams p{};
     p.q = q; p.T = T; p.position = position; p.kv_begin = 0; p.kv_rows = kv_rows;
     p.mode = 1; p.direct = 1; p.out = out; p.lse = lse; p.splits = 1;
-    fa_kernel<<<dim3(NQ, (T + BM - 1) / BM), 256, SMEM_BYTES, st>>>(mk, mv, p);
+    constexpr int R = FaLayout<false>::QROWS;
+    launch_fa<false>(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
     check_launch("prefill attention");
 }
 

@@ -1,19 +1,23 @@
 // Gated DeltaNet recurrent path for sm_100a: one fused kernel per layer call.
 //
 // The reference runs conv -> gdn_prep -> gdn_scan -> delta_out as four
-// launches (src/kernels.cu:275-354, 409-414, 557-566).  Here one CTA owns one
-// value head: it recomputes the causal conv + SiLU of the q/k channels of its
-// key head (h % Hk) and of its own v channels, L2-normalises q and k, forms
-// the decay a = exp(A softplus(alpha+bias)) and beta = sigmoid(beta), runs the
-// delta rule over the tokens with the head's 128x128 fp32 state held in
-// registers (4 threads per state row, 32 columns each), and applies the gated
-// RMSNorm before writing the output.  The state is read and written exactly
-// once per call.
+// launches (src/kernels.cu:275-354, 409-414, 557-566).  Here a cluster of
+// CPH CTAs owns one value head; each CTA owns D/CPH rows of the head's
+// [Dv][Dk] fp32 state (4 threads per row, D/4 columns each, in registers).
+// Every CTA recomputes the causal conv + SiLU of the q/k channels of its key
+// head (h % Hk) and of its own v rows, L2-normalises q and k, forms the decay
+// a = exp(A softplus(alpha+bias)) and beta = sigmoid(beta), and runs the delta
+// rule over the tokens.  The gated RMSNorm needs the whole head's readout:
+// the per-CTA sums of squares are exchanged through distributed shared
+// memory.  The state is read and written exactly once per call.
 #include "common.cuh"
 #include "hotpath.h"
 
+#include <cooperative_groups.h>
 #include <stdexcept>
 #include <string>
+
+namespace cg = cooperative_groups;
 
 namespace qv {
 
@@ -29,62 +33,91 @@ struct DeltaArgs {
 };
 
 // CORE = false: reference layer semantics (conv, SiLU, gated RMSNorm).
-// CORE = true : prepared-input recurrence used by the chunked-prefill path
-//               (raw fp16 q/k/v are L2-normalised here; output is the state
-//               readout before the gated norm).
-template <int D, bool CORE>
-__global__ void __launch_bounds__(D * 4)
+// CORE = true : prepared-input recurrence (raw fp16 q/k/v are L2-normalised
+//               here; the output is the state readout before the gated norm).
+template <int D, int CPH, bool CORE>
+__global__ void __cluster_dims__(CPH, 1, 1) __launch_bounds__(128)
 delta_kernel(const DeltaArgs a) {
-    constexpr int NT = D * 4, COLS = D / 4, NV4 = D / 16, NW = NT / 32;
-    const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int ROWS = D / CPH;                 // state rows of this CTA
+    constexpr int NT = ROWS * 4;                  // 4 threads per row
+    static_assert(NT == 128, "one 128-thread CTA per cluster rank");
+    constexpr int COLS = D / 4, NV4 = D / 16, NW = NT / 32;
+    constexpr int NCH = 2 * D + ROWS;             // q, k channels of the key head + own v rows
+    constexpr int CPT = (NCH + NT - 1) / NT;      // conv channels per thread
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = CPH > 1 ? (int)cluster.block_rank() : 0;
+    const int h = blockIdx.x / CPH, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int Hk = a.Hk, Hv = a.Hv, kh = h % Hk;
     const int C = (2 * Hk + Hv) * D;
-    const int r = tid >> 2, j = tid & 3;
+    const int r = tid >> 2, j = tid & 3;          // local row, column quarter
+    const int row0 = rank * ROWS;                 // first head row of this CTA
 
-    __shared__ __align__(16) float F[3][CHUNK][D];   // q, k, v (filtered)
-    __shared__ __align__(16) float O[CHUNK][D];
+    __shared__ __align__(16) float Fq[CHUNK][D], Fk[CHUNK][D], Fv[CHUNK][ROWS];
+    __shared__ __align__(16) float O[CHUNK][ROWS];
     __shared__ float sa[CHUNK], sb[CHUNK], sq[CHUNK], sk[CHUNK];
+    __shared__ float psum[2][CHUNK];              // per-CTA sum of squares, double-buffered by chunk
 
     // State row fragment: columns 16*i + 4*j + e.
     float S[COLS];
-    float *srow = a.state + ((size_t)h * D + r) * D;
+    float *srow = a.state + ((size_t)h * D + row0 + r) * D;
 #pragma unroll
     for (int i = 0; i < NV4; ++i) {
         const float4 v = *reinterpret_cast<const float4 *>(srow + 16 * i + 4 * j);
         S[4 * i] = v.x; S[4 * i + 1] = v.y; S[4 * i + 2] = v.z; S[4 * i + 3] = v.w;
     }
 
-    // Conv channel owned by this thread (tid < 3D): 0 = q, 1 = k, 2 = v.
-    const int ctype = tid / D, cidx = tid % D;
-    int c = -1;
-    if (ctype == 0) c = kh * D + cidx;
-    else if (ctype == 1) c = (Hk + kh) * D + cidx;
-    else if (ctype == 2) c = (2 * Hk + h) * D + cidx;
-    float w0 = 0, w1 = 0, w2 = 0, w3 = 0, h0 = 0, h1 = 0, h2 = 0;
-    if (!CORE && c >= 0) {
-        w0 = a.conv[(size_t)c * 4]; w1 = a.conv[(size_t)c * 4 + 1];
-        w2 = a.conv[(size_t)c * 4 + 2]; w3 = a.conv[(size_t)c * 4 + 3];
-        h0 = a.history[c]; h1 = a.history[(size_t)C + c]; h2 = a.history[2 * (size_t)C + c];
+    // Conv channels of this thread: index e < 2D -> q/k channel of key head kh,
+    // else v channel of row row0 + (e - 2D).  Window registers persist across chunks.
+    int ch[CPT];
+    float w0[CPT], w1[CPT], w2[CPT], w3[CPT], h0[CPT], h1[CPT], h2[CPT];
+#pragma unroll
+    for (int u = 0; u < CPT; ++u) {
+        const int e = tid + u * NT;
+        int c = -1;
+        if (e < D) c = kh * D + e;
+        else if (e < 2 * D) c = (Hk + kh) * D + (e - D);
+        else if (e < NCH) c = (2 * Hk + h) * D + row0 + (e - 2 * D);
+        ch[u] = c;
+        w0[u] = w1[u] = w2[u] = w3[u] = h0[u] = h1[u] = h2[u] = 0.f;
+        if (!CORE && c >= 0) {
+            const float4 w = *reinterpret_cast<const float4 *>(a.conv + (size_t)c * 4);
+            w0[u] = w.x; w1[u] = w.y; w2[u] = w.z; w3[u] = w.w;
+            h0[u] = a.history[c]; h1[u] = a.history[(size_t)C + c]; h2[u] = a.history[2 * (size_t)C + c];
+        }
     }
 
-    for (int t0 = 0; t0 < a.T; t0 += CHUNK) {
+    for (int t0 = 0, chunk = 0; t0 < a.T; t0 += CHUNK, ++chunk) {
         const int n = min(CHUNK, a.T - t0);
-        if (c >= 0) {
-            for (int tt = 0; tt < n; ++tt) {
-                float f;
-                if (!CORE) {
-                    const float raw = a.qkv[(size_t)(t0 + tt) * C + c];
-                    float v = w3 * raw;
-                    v += w0 * h0; v += w1 * h1; v += w2 * h2;
-                    h0 = h1; h1 = h2; h2 = raw;
-                    f = siluf_(v);
-                } else {
+        // -------- conv + SiLU (all loads of the chunk issued before use)
+#pragma unroll
+        for (int u = 0; u < CPT; ++u) {
+            const int e = tid + u * NT, c = ch[u];
+            if (c < 0) continue;
+            float raw[CHUNK];
+#pragma unroll
+            for (int tt = 0; tt < CHUNK; ++tt) {
+                raw[tt] = 0.f;
+                if (tt < n) {
                     const int t = t0 + tt;
-                    f = ctype == 0 ? __half2float(a.q16[((size_t)t * Hk + kh) * D + cidx])
-                      : ctype == 1 ? __half2float(a.k16[((size_t)t * Hk + kh) * D + cidx])
-                                   : __half2float(a.v16[((size_t)t * Hv + h) * D + cidx]);
+                    if (!CORE) raw[tt] = a.qkv[(size_t)t * C + c];
+                    else if (e < D) raw[tt] = __half2float(a.q16[((size_t)t * Hk + kh) * D + e]);
+                    else if (e < 2 * D) raw[tt] = __half2float(a.k16[((size_t)t * Hk + kh) * D + e - D]);
+                    else raw[tt] = __half2float(a.v16[((size_t)t * Hv + h) * D + row0 + e - 2 * D]);
                 }
-                F[ctype][tt][cidx] = f;
+            }
+#pragma unroll
+            for (int tt = 0; tt < CHUNK; ++tt) {
+                if (tt >= n) break;
+                float f = raw[tt];
+                if (!CORE) {
+                    float v = w3[u] * raw[tt];
+                    v += w0[u] * h0[u]; v += w1[u] * h1[u]; v += w2[u] * h2[u];
+                    h0[u] = h1[u]; h1[u] = h2[u]; h2[u] = raw[tt];
+                    f = siluf_(v);
+                }
+                if (e < D) Fq[tt][e] = f;
+                else if (e < 2 * D) Fk[tt][e - D] = f;
+                else Fv[tt][e - 2 * D] = f;
             }
         }
         if (tid < n) {
@@ -93,26 +126,30 @@ delta_kernel(const DeltaArgs a) {
             sb[tid] = sigmoidf_(a.beta[idx]);
         }
         __syncthreads();
+        // -------- L2 norms of q and k (q also by 1/sqrt(D))
         for (int task = warp; task < 2 * n; task += NW) {
-            const int tt = task >> 1, which = task & 1;
+            const int tt = task >> 1;
+            const float *src = (task & 1) ? Fk[tt] : Fq[tt];
             float s = 0.f;
-            for (int i = lane; i < D; i += 32) { const float x = F[which][tt][i]; s += x * x; }
+#pragma unroll
+            for (int i = lane; i < D; i += 32) s += src[i] * src[i];
             s = warp_sum(s);
             if (lane == 0) {
-                if (which == 0) sq[tt] = rsqrtf(s + 1e-6f) * rsqrtf((float)D);
-                else sk[tt] = rsqrtf(s + 1e-6f);
+                if (task & 1) sk[tt] = rsqrtf(s + 1e-6f);
+                else sq[tt] = rsqrtf(s + 1e-6f) * rsqrtf((float)D);
             }
         }
         __syncthreads();
         for (int e = tid; e < n * D; e += NT) {
             const int tt = e / D, i = e % D;
-            F[0][tt][i] *= sq[tt];
-            F[1][tt][i] *= sk[tt];
+            Fq[tt][i] *= sq[tt];
+            Fk[tt][i] *= sk[tt];
         }
         __syncthreads();
+        // -------- delta rule: S = a S; u = S k; delta = beta (v - u); S += delta k^T; o = S q
         for (int tt = 0; tt < n; ++tt) {
             const float decay = sa[tt], beta = sb[tt];
-            const float *kk = F[1][tt], *qq = F[0][tt];
+            const float *kk = Fk[tt], *qq = Fq[tt];
             float u0 = 0.f, u1 = 0.f;
 #pragma unroll
             for (int i = 0; i < NV4; ++i) {
@@ -124,7 +161,7 @@ delta_kernel(const DeltaArgs a) {
             float u = u0 + u1;
             u += __shfl_xor_sync(0xffffffffu, u, 1);
             u += __shfl_xor_sync(0xffffffffu, u, 2);
-            const float delta = (F[2][tt][r] - u) * beta;
+            const float delta = (Fv[tt][r] - u) * beta;
             float o0 = 0.f, o1 = 0.f;
 #pragma unroll
             for (int i = 0; i < NV4; ++i) {
@@ -142,31 +179,49 @@ delta_kernel(const DeltaArgs a) {
         }
         __syncthreads();
         if (CORE) {
-            for (int e = tid; e < n * D; e += NT) {
-                const int tt = e / D, i = e % D;
-                a.out[((size_t)(t0 + tt) * Hv + h) * D + i] = O[tt][i];
+            for (int e = tid; e < n * ROWS; e += NT) {
+                const int tt = e / ROWS, i = e % ROWS;
+                a.out[((size_t)(t0 + tt) * Hv + h) * D + row0 + i] = O[tt][i];
             }
         } else {
+            // -------- gated RMSNorm over the whole head (cluster-wide sum of squares)
+            float *ps = psum[chunk & 1];
             for (int tt = warp; tt < n; tt += NW) {
                 float s = 0.f;
-                for (int i = lane; i < D; i += 32) s += O[tt][i] * O[tt][i];
-                const float scale = rsqrtf(warp_sum(s) / D + a.eps);
-                const size_t base = ((size_t)(t0 + tt) * Hv + h) * D;
-                for (int i = lane; i < D; i += 32)
-                    a.out[base + i] = O[tt][i] * scale * a.norm[i] * siluf_(a.gate[base + i]);
+                for (int i = lane; i < ROWS; i += 32) s += O[tt][i] * O[tt][i];
+                s = warp_sum(s);
+                if (lane == 0) ps[tt] = s;
+            }
+            if (CPH > 1) cluster.sync(); else __syncthreads();
+            for (int e = tid; e < n * ROWS; e += NT) {
+                const int tt = e / ROWS, i = e % ROWS;
+                float total = 0.f;
+#pragma unroll
+                for (int q = 0; q < CPH; ++q)
+                    total += CPH > 1 ? cluster.map_shared_rank(ps, q)[tt] : ps[tt];
+                const float scale = rsqrtf(total / D + a.eps);
+                const size_t o = ((size_t)(t0 + tt) * Hv + h) * D + row0 + i;
+                a.out[o] = O[tt][i] * scale * a.norm[row0 + i] * siluf_(a.gate[o]);
             }
         }
         __syncthreads();
     }
+    // No CTA may leave while a peer can still read its psum.
+    if (!CORE && CPH > 1) cluster.sync();
 
 #pragma unroll
     for (int i = 0; i < NV4; ++i)
         *reinterpret_cast<float4 *>(srow + 16 * i + 4 * j) =
             make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
-    // History rows: v channels belong to this head; the q/k channels of key
-    // head kh are written by value head kh (h < Hk) only.
-    if (!CORE && c >= 0 && (ctype == 2 || h < Hk)) {
-        a.history[c] = h0; a.history[(size_t)C + c] = h1; a.history[2 * (size_t)C + c] = h2;
+    // History rows: v channels belong to their rows' CTA; the q/k channels of
+    // key head kh are written by rank 0 of value head kh (h < Hk) only.
+    if (!CORE) {
+#pragma unroll
+        for (int u = 0; u < CPT; ++u) {
+            const int e = tid + u * NT, c = ch[u];
+            if (c < 0 || (e < 2 * D && !(h < Hk && rank == 0))) continue;
+            a.history[c] = h0[u]; a.history[(size_t)C + c] = h1[u]; a.history[2 * (size_t)C + c] = h2[u];
+        }
     }
 }
 
@@ -177,6 +232,7 @@ void check_launch(const char *what) {
 }
 }  // namespace
 
+// D = 128: 4-CTA clusters per value head (32 state rows per CTA); D = 32: one CTA.
 void delta_run(float *out, float *state, float *history, const float *qkv, const float *gate,
                const float *alpha, const float *beta, const float *conv, const float *decay,
                const float *bias, const float *norm, int T, int Hk, int Hv, int D, float eps,
@@ -185,8 +241,8 @@ void delta_run(float *out, float *state, float *history, const float *qkv, const
     a.out = out; a.state = state; a.history = history; a.qkv = qkv; a.gate = gate;
     a.alpha = alpha; a.beta = beta; a.conv = conv; a.decay = decay; a.bias = bias; a.norm = norm;
     a.T = T; a.Hk = Hk; a.Hv = Hv; a.eps = eps;
-    if (D == 128) delta_kernel<128, false><<<Hv, 512, 0, st>>>(a);
-    else if (D == 32) delta_kernel<32, false><<<Hv, 128, 0, st>>>(a);
+    if (D == 128) delta_kernel<128, 4, false><<<Hv * 4, 128, 0, st>>>(a);
+    else if (D == 32) delta_kernel<32, 1, false><<<Hv, 128, 0, st>>>(a);
     else throw std::invalid_argument("unsupported DeltaNet dimension");
     check_launch("delta");
 }
@@ -198,8 +254,8 @@ void delta_core_recurrent(float *out, float *state, const __half *q, const __hal
     a.out = out; a.state = state; a.q16 = q; a.k16 = k; a.v16 = v;
     a.alpha = alpha; a.beta = beta; a.decay = decay; a.bias = bias;
     a.T = T; a.Hk = Hk; a.Hv = Hv;
-    if (D == 128) delta_kernel<128, true><<<Hv, 512, 0, st>>>(a);
-    else if (D == 32) delta_kernel<32, true><<<Hv, 128, 0, st>>>(a);
+    if (D == 128) delta_kernel<128, 4, true><<<Hv * 4, 128, 0, st>>>(a);
+    else if (D == 32) delta_kernel<32, 1, true><<<Hv, 128, 0, st>>>(a);
     else throw std::invalid_argument("unsupported DeltaNet dimension");
     check_launch("delta core");
 }

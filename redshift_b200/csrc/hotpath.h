@@ -10,6 +10,7 @@ namespace qv {
 
 // Attention (attention.cu).  Cache layout [rows][4][256] fp16.
 size_t attention_workspace_bytes(int T, int kv_rows);
+int attention_max_shard_batch();   // largest batch of the split-KV (decode) regime
 void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const float *q_gate,
                    const float *key, const float *value, const float *qn, const float *kn, int T,
                    int position, int kv_begin, int kv_rows, bool append, float eps, void *ws,

@@ -321,7 +321,7 @@ int qv_delta(float *out, float *state, float *history, const float *qkv, const f
 }
 
 size_t qv_attention_shard_workspace(int batch, int shard_rows) {
-    if (batch < 1 || batch > 21 || shard_rows < 0) return 0;
+    if (batch < 1 || batch > qv::attention_max_shard_batch() || shard_rows < 0) return 0;
     // The split plan is not monotone in the row count: cover both cases.
     const size_t a = qv::attention_workspace_bytes(batch, shard_rows + batch);
     const size_t b = shard_rows ? qv::attention_workspace_bytes(batch, shard_rows) : 0;
@@ -333,7 +333,7 @@ int qv_attention_shard(float *partial, float *lse, void *key_cache, void *value_
                        const float *q_norm, const float *k_norm, int batch, int position, float epsilon,
                        void *workspace, size_t workspace_bytes, void *stream) {
     return guarded([&] {
-        require(batch >= 1 && batch <= 21, "shard batch must be between 1 and 21");
+        require(batch >= 1 && batch <= qv::attention_max_shard_batch(), "shard batch must be between 1 and 10");
         check_epsilon(epsilon);
         require(position >= 0 && position <= kMaxContext - batch, "attention context exceeds 139264");
         require(shard_begin >= 0 && shard_rows >= 0, "invalid shard range");

@@ -117,7 +117,7 @@ def test_device_entry_points_validate_first(lib):
     v = ct.c_void_p(8)   # never dereferenced: validation fails first
     assert lib.qv_attention_workspace(0, 0) == 0
     assert lib.qv_attention(v, v, v, v, v, v, v, v, 1, 139264, 1e-6, v, 1, None) == -1
-    assert lib.qv_attention_shard(v, v, v, v, 0, 10, v, v, v, v, v, 22, 100, 1e-6, v, 1, None) == -1
+    assert lib.qv_attention_shard(v, v, v, v, 0, 10, v, v, v, v, v, 11, 100, 1e-6, v, 1, None) == -1
     assert lib.qv_attention_shard(v, v, v, v, 0, 101, v, v, v, v, v, 1, 100, 1e-6, v, 1, None) == -1
     assert b'past the verify position' in lib.qv_error()
     assert lib.qv_attention_merge(v, v, v, 0, 1, v, None) == -1
