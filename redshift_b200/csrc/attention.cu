@@ -268,13 +268,14 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             float m_tile = -INFINITY;
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
-                x[c] = c <= lim ? x[c] * SCORE_LOG2 : -INFINITY;
+                x[c] = c <= lim ? x[c] : -INFINITY;
                 m_tile = fmaxf(m_tile, x[c]);
             }
             if (PRECISE) m_tile = fmaxf(m_tile, __shfl_xor_sync(0xffffffffu, m_tile, 16));
+            m_tile *= SCORE_LOG2;                                  // log2 units (-inf stays -inf)
             float factor = 1.f;
             const bool need = m_tile > m_use + RESCALE_THRESHOLD;
-            if (need) { factor = exp2f(m_use - m_tile); m_use = m_tile; l *= factor; }
+            if (need) { factor = exp2_approx(m_use - m_tile); m_use = m_tile; l *= factor; }
             if (j > 0 && __any_sync(0xffffffffu, need)) {
                 // O already holds tiles < j: wait for PV(j-1), then rescale rows in TMEM.
                 if (!warp_wait(p_free + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
@@ -295,17 +296,16 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             float sum = 0.f;
 #pragma unroll
             for (int c = 0; c < NC; c += 2) {
-                const float p0 = exp2f(x[c] - mref), p1 = exp2f(x[c + 1] - mref);
+                const float p0 = exp2_approx(fmaf(x[c], SCORE_LOG2, -mref));
+                const float p1 = exp2_approx(fmaf(x[c + 1], SCORE_LOG2, -mref));
                 const __half2 hp = __floats2half2_rn(p0, p1);
                 hi[c / 2] = *reinterpret_cast<const uint32_t *>(&hp);
-                const float2 back = __half22float2(hp);
                 if (PRECISE) {
+                    const float2 back = __half22float2(hp);
                     const __half2 lp = __floats2half2_rn(p0 - back.x, p1 - back.y);
                     lo[c / 2] = *reinterpret_cast<const uint32_t *>(&lp);
-                    sum += p0 + p1;
-                } else {
-                    sum += back.x + back.y;
                 }
+                sum += p0 + p1;
             }
             l += sum;
             if (j >= 2 && !warp_wait(p_free + b, ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
@@ -448,7 +448,7 @@ attn_combine_kernel(float *out, float *out_lse, const float *part_o, const float
     __syncthreads();
     M = fmaxf(red[0], red[1]);
     const float w = (d < splits && m != -INFINITY) ? exp2f(m - M) : 0.f;
-    if (d < MAX_SPLITS) wgt[d] = w;
+    if (d < MAX_SPLITS) wgt[d] = w;     // zero for d >= splits
     float den = w * l;
 #pragma unroll
     for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
@@ -458,15 +458,15 @@ attn_combine_kernel(float *out, float *out_lse, const float *part_o, const float
     if (d == 0) den_s = red[0] + red[1];
     __syncthreads();
     den = den_s;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // Every split's value is loaded before any is used: one memory round trip.
     const float *src = part_o + slot0 * HD + d;
-    int s = 0;
-    for (; s + 8 <= splits; s += 8) {
+    float v[MAX_SPLITS];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += wgt[s + e] * src[(size_t)(s + e) * DECODE_ROWS * HD];
-    }
-    for (; s < splits; ++s) acc[0] += wgt[s] * src[(size_t)s * DECODE_ROWS * HD];
-    const float num = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+    for (int e = 0; e < MAX_SPLITS; ++e) v[e] = e < splits ? src[(size_t)e * DECODE_ROWS * HD] : 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int e = 0; e < MAX_SPLITS; ++e) acc[e & 3] += wgt[e] * v[e];
+    const float num = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     const size_t o = ((size_t)t * NQ + h) * HD + d;
     if (final_gate) {
         out[o] = (den > 0.f ? num / den : 0.f) * sigmoidf_(q_gate[((size_t)t * NQ + h) * 2 * HD + HD + d]);

@@ -63,6 +63,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
+// Cluster (DSMEM) helpers: address of the same shared variable in CTA `rank`
+// of the cluster, a store there, and a release-arrive on a peer's mbarrier.
+__device__ __forceinline__ uint32_t cluster_map(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" :: "r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(remote_bar) : "memory");
+}
+// Bounded acquire-wait (cluster scope) on a local mbarrier that peers arrive on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity) {
+    const long long start = clock64();
+    while (true) {
+        uint32_t ok;
+        asm volatile("{\n\t.reg .pred p;\n\t"
+                     "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+        if (ok) return true;
+        if (clock64() - start > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); return false; }
+    }
+}
+
 // ---------------------------------------------------------------- proxies
 __device__ __forceinline__ void fence_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -193,6 +220,12 @@ __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
     for (int d = 16; d; d >>= 1) x += __shfl_xor_sync(0xffffffffu, x, d);
     return x;
+}
+// 2^x with the SFU's approximate exp2 (flushes subnormal results to zero).
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x * sigmoidf_(x); }

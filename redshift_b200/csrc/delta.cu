@@ -3,13 +3,12 @@
 // The reference runs conv -> gdn_prep -> gdn_scan -> delta_out as four
 // launches (src/kernels.cu:275-354, 409-414, 557-566).  Here a cluster of
 // CPH CTAs owns one value head; each CTA owns D/CPH rows of the head's
-// [Dv][Dk] fp32 state (4 threads per row, D/4 columns each, in registers).
-// Every CTA recomputes the causal conv + SiLU of the q/k channels of its key
-// head (h % Hk) and of its own v rows, L2-normalises q and k, forms the decay
-// a = exp(A softplus(alpha+bias)) and beta = sigmoid(beta), and runs the delta
-// rule over the tokens.  The gated RMSNorm needs the whole head's readout:
-// the per-CTA sums of squares are exchanged through distributed shared
-// memory.  The state is read and written exactly once per call.
+// [Dv][Dk] fp32 state, held in registers.  The cluster filters (causal conv
+// + SiLU) the q/k channels of its key head (h % Hk) and its v rows, forms the
+// L2 norms, the decay a = exp(A softplus(alpha+bias)) and beta = sigmoid(beta),
+// and runs the delta rule over the tokens.  The gated RMSNorm needs the whole
+// head's readout: the per-CTA sums of squares are exchanged through
+// distributed shared memory.  The state is read and written exactly once.
 #include "common.cuh"
 #include "hotpath.h"
 
@@ -35,193 +34,236 @@ struct DeltaArgs {
 // CORE = false: reference layer semantics (conv, SiLU, gated RMSNorm).
 // CORE = true : prepared-input recurrence (raw fp16 q/k/v are L2-normalised
 //               here; the output is the state readout before the gated norm).
+//
+// Grid: CPH CTAs per value head (a cluster); every CTA must own an SM, since
+// an SM holding two CTAs would double the time of its whole cluster.
+// Thread layout: 8 threads per state row, D/8 columns each (columns
+// 32i + 4j + e), so a row's dot products reduce with 3 shuffles; every thread
+// also filters one conv channel.  Per chunk of <= 8 tokens:
+//  * the chunk's inputs are loaded one chunk ahead (chunk 0 with the
+//    prologue), so their latency overlaps the previous chunk's scan;
+//  * each CTA filters (conv + SiLU) all q/k channels of its key head and its
+//    own v rows, so the q/k L2 norms need no cross-CTA exchange; the norms
+//    are applied as scalars inside the dot products (u = sk*(S.k),
+//    o = sq*(S.q), the rank-1 update uses sk*delta);
+//  * the gated RMSNorm's per-token sum of squares is the only cross-CTA
+//    value: every CTA pushes its partial into each peer's shared memory and
+//    arrives on the peer's mbarrier (one-way, no cluster-wide barrier).
+// D=128 uses CPH=2 (64 rows, 512 threads): clusters must fit inside one GPC,
+// and 48 clusters of 3 do not all fit at once on B200, which then runs a
+// second wave; clusters of 2 always fit (one CTA per SM, 96 SMs).
+template <int D, int CPH> struct DeltaShape {
+    static constexpr int MAXR = (D + CPH - 1) / CPH;              // most rows of a rank
+    static constexpr int NT = ((MAXR * 8 + 31) / 32) * 32;         // threads per CTA
+};
+
 template <int D, int CPH, bool CORE>
-__global__ void __cluster_dims__(CPH, 1, 1) __launch_bounds__(128)
+__global__ void __cluster_dims__(CPH, 1, 1) __launch_bounds__(DeltaShape<D, CPH>::NT)
 delta_kernel(const DeltaArgs a) {
-    constexpr int ROWS = D / CPH;                 // state rows of this CTA
-    constexpr int NT = ROWS * 4;                  // 4 threads per row
-    static_assert(NT == 128, "one 128-thread CTA per cluster rank");
-    constexpr int COLS = D / 4, NV4 = D / 16, NW = NT / 32;
-    constexpr int NCH = 2 * D + ROWS;             // q, k channels of the key head + own v rows
-    constexpr int CPT = (NCH + NT - 1) / NT;      // conv channels per thread
+    constexpr int MAXR = DeltaShape<D, CPH>::MAXR, NT = DeltaShape<D, CPH>::NT;
+    constexpr int NV4 = D / 32, COLS = D / 8, NW = NT / 32;
+    static_assert(2 * D + MAXR <= NT, "one conv channel per thread");
+    static_assert(CHUNK * MAXR <= NT, "one output per thread per chunk");
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = CPH > 1 ? (int)cluster.block_rank() : 0;
     const int h = blockIdx.x / CPH, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int Hk = a.Hk, Hv = a.Hv, kh = h % Hk;
     const int C = (2 * Hk + Hv) * D;
-    const int r = tid >> 2, j = tid & 3;          // local row, column quarter
-    const int row0 = rank * ROWS;                 // first head row of this CTA
+    const int row0 = rank * D / CPH, rows = (rank + 1) * D / CPH - row0;   // this CTA's head rows
+    const int r = tid >> 3, j = tid & 7;          // local row, column group
+    const bool has_row = r < rows;
 
-    __shared__ __align__(16) float Fq[CHUNK][D], Fk[CHUNK][D], Fv[CHUNK][ROWS];
-    __shared__ __align__(16) float O[CHUNK][ROWS];
-    __shared__ float sa[CHUNK], sb[CHUNK], sq[CHUNK], sk[CHUNK];
-    __shared__ float psum[2][CHUNK];              // per-CTA sum of squares, double-buffered by chunk
+    __shared__ __align__(16) float Fq[CHUNK][D], Fk[CHUNK][D], Fv[CHUNK][MAXR];
+    __shared__ __align__(16) float O[CHUNK][MAXR];
+    __shared__ float wsum[NW][CHUNK];             // per-warp sums of q^2 or k^2
+    __shared__ float scal[CHUNK][4];              // sq, sk, decay, beta
+    __shared__ float osum[2][CPH][CHUNK];         // sums of o^2 pushed by each rank, by chunk parity
+    __shared__ __align__(8) uint64_t osum_bar[2];
+    __shared__ bool norm_ok;
 
-    // State row fragment: columns 16*i + 4*j + e.
+    if (!CORE && tid == 0) {
+        // each rank's CHUNK token-warps arrive once per chunk
+        mbar_init(&osum_bar[0], CPH * CHUNK);
+        mbar_init(&osum_bar[1], CPH * CHUNK);
+        fence_barrier_init();
+    }
+
+    // ---- loads that do not depend on the chunk
     float S[COLS];
-    float *srow = a.state + ((size_t)h * D + row0 + r) * D;
+    float *srow = a.state + ((size_t)h * D + row0 + (has_row ? r : 0)) * D;
 #pragma unroll
     for (int i = 0; i < NV4; ++i) {
-        const float4 v = *reinterpret_cast<const float4 *>(srow + 16 * i + 4 * j);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has_row) v = *reinterpret_cast<const float4 *>(srow + 32 * i + 4 * j);
         S[4 * i] = v.x; S[4 * i + 1] = v.y; S[4 * i + 2] = v.z; S[4 * i + 3] = v.w;
     }
-
-    // Conv channels of this thread: index e < 2D -> q/k channel of key head kh,
-    // else v channel of row row0 + (e - 2D).  Window registers persist across chunks.
-    int ch[CPT];
-    float w0[CPT], w1[CPT], w2[CPT], w3[CPT], h0[CPT], h1[CPT], h2[CPT];
-#pragma unroll
-    for (int u = 0; u < CPT; ++u) {
-        const int e = tid + u * NT;
-        int c = -1;
-        if (e < D) c = kh * D + e;
-        else if (e < 2 * D) c = (Hk + kh) * D + (e - D);
-        else if (e < NCH) c = (2 * Hk + h) * D + row0 + (e - 2 * D);
-        ch[u] = c;
-        w0[u] = w1[u] = w2[u] = w3[u] = h0[u] = h1[u] = h2[u] = 0.f;
-        if (!CORE && c >= 0) {
-            const float4 w = *reinterpret_cast<const float4 *>(a.conv + (size_t)c * 4);
-            w0[u] = w.x; w1[u] = w.y; w2[u] = w.z; w3[u] = w.w;
-            h0[u] = a.history[c]; h1[u] = a.history[(size_t)C + c]; h2[u] = a.history[2 * (size_t)C + c];
-        }
+    // Conv channel of this thread: e < D -> q, e < 2D -> k, e < 2D + rows -> v row.
+    const int e = tid;
+    int c = -1;
+    if (e < D) c = kh * D + e;
+    else if (e < 2 * D) c = (Hk + kh) * D + (e - D);
+    else if (e < 2 * D + rows) c = (2 * Hk + h) * D + row0 + (e - 2 * D);
+    float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f, h0 = 0.f, h1 = 0.f, h2 = 0.f;
+    if (!CORE && c >= 0) {
+        const float4 w = *reinterpret_cast<const float4 *>(a.conv + (size_t)c * 4);
+        w0 = w.x; w1 = w.y; w2 = w.z; w3 = w.w;
+        h0 = a.history[c]; h1 = a.history[(size_t)C + c]; h2 = a.history[2 * (size_t)C + c];
     }
+    const float decay_h = a.decay[h], bias_h = a.bias[h];
+    // Output of this thread in each chunk: token tid / rows, row tid % rows.
+    const bool has_out = tid < CHUNK * rows;
+    const int out_t = has_out ? tid / rows : 0, out_i = has_out ? tid % rows : 0;
+    const float nw = (!CORE && has_out) ? a.norm[row0 + out_i] : 1.f;
+
+    // Chunk inputs are prefetched one chunk ahead (chunk 0 with the prologue).
+    float raw_n[CHUNK], al_n = 0.f, be_n = 0.f, gz_n = 0.f;
+    auto load_chunk = [&](int c0) {
+        const int m = min(CHUNK, a.T - c0);
+#pragma unroll
+        for (int tt = 0; tt < CHUNK; ++tt) {
+            raw_n[tt] = 0.f;
+            if (c >= 0 && tt < m) {
+                const int t = c0 + tt;
+                if (!CORE) raw_n[tt] = a.qkv[(size_t)t * C + c];
+                else if (e < D) raw_n[tt] = __half2float(a.q16[((size_t)t * Hk + kh) * D + e]);
+                else if (e < 2 * D) raw_n[tt] = __half2float(a.k16[((size_t)t * Hk + kh) * D + e - D]);
+                else raw_n[tt] = __half2float(a.v16[((size_t)t * Hv + h) * D + row0 + e - 2 * D]);
+            }
+        }
+        if (tid < m) {
+            const size_t idx = (size_t)(c0 + tid) * Hv + h;
+            al_n = a.alpha[idx];
+            be_n = a.beta[idx];
+        }
+        gz_n = (!CORE && has_out && out_t < m) ? a.gate[((size_t)(c0 + out_t) * Hv + h) * D + row0 + out_i] : 0.f;
+    };
+    load_chunk(0);
+    // Peers arrive on osum_bar only after it is initialised everywhere.
+    if (!CORE && CPH > 1) cluster.sync();
 
     for (int t0 = 0, chunk = 0; t0 < a.T; t0 += CHUNK, ++chunk) {
         const int n = min(CHUNK, a.T - t0);
-        // -------- conv + SiLU (all loads of the chunk issued before use)
+        // ---- this chunk's inputs were prefetched; start the next chunk's loads
+        float raw[CHUNK];
 #pragma unroll
-        for (int u = 0; u < CPT; ++u) {
-            const int e = tid + u * NT, c = ch[u];
-            if (c < 0) continue;
-            float raw[CHUNK];
+        for (int tt = 0; tt < CHUNK; ++tt) raw[tt] = raw_n[tt];
+        const float al = al_n, be = be_n, gz = gz_n;
+        if (t0 + CHUNK < a.T) load_chunk(t0 + CHUNK);
+        // ---- conv + SiLU in registers; per-warp sums of squares of q (warps
+        //      [0, D/32)) and k (warps [D/32, 2D/32))
+        float sq2[CHUNK];
 #pragma unroll
-            for (int tt = 0; tt < CHUNK; ++tt) {
-                raw[tt] = 0.f;
-                if (tt < n) {
-                    const int t = t0 + tt;
-                    if (!CORE) raw[tt] = a.qkv[(size_t)t * C + c];
-                    else if (e < D) raw[tt] = __half2float(a.q16[((size_t)t * Hk + kh) * D + e]);
-                    else if (e < 2 * D) raw[tt] = __half2float(a.k16[((size_t)t * Hk + kh) * D + e - D]);
-                    else raw[tt] = __half2float(a.v16[((size_t)t * Hv + h) * D + row0 + e - 2 * D]);
-                }
+        for (int tt = 0; tt < CHUNK; ++tt) {
+            float f = raw[tt];
+            if (!CORE && tt < n) {
+                float v = w3 * f;
+                v += w0 * h0; v += w1 * h1; v += w2 * h2;
+                h0 = h1; h1 = h2; h2 = f;
+                f = siluf_(v);
             }
-#pragma unroll
-            for (int tt = 0; tt < CHUNK; ++tt) {
-                if (tt >= n) break;
-                float f = raw[tt];
-                if (!CORE) {
-                    float v = w3[u] * raw[tt];
-                    v += w0[u] * h0[u]; v += w1[u] * h1[u]; v += w2[u] * h2[u];
-                    h0[u] = h1[u]; h1[u] = h2[u]; h2[u] = raw[tt];
-                    f = siluf_(v);
-                }
-                if (e < D) Fq[tt][e] = f;
-                else if (e < 2 * D) Fk[tt][e - D] = f;
+            sq2[tt] = 0.f;
+            if (c >= 0 && tt < n) {
+                if (e < D) { Fq[tt][e] = f; sq2[tt] = f * f; }
+                else if (e < 2 * D) { Fk[tt][e - D] = f; sq2[tt] = f * f; }
                 else Fv[tt][e - 2 * D] = f;
             }
         }
-        if (tid < n) {
-            const size_t idx = (size_t)(t0 + tid) * Hv + h;
-            sa[tid] = expf(a.decay[h] * softplusf_(a.alpha[idx] + a.bias[h]));
-            sb[tid] = sigmoidf_(a.beta[idx]);
-        }
-        __syncthreads();
-        // -------- L2 norms of q and k (q also by 1/sqrt(D))
-        for (int task = warp; task < 2 * n; task += NW) {
-            const int tt = task >> 1;
-            const float *src = (task & 1) ? Fk[tt] : Fq[tt];
-            float s = 0.f;
+        if (warp < 2 * D / 32) {
 #pragma unroll
-            for (int i = lane; i < D; i += 32) s += src[i] * src[i];
-            s = warp_sum(s);
-            if (lane == 0) {
-                if (task & 1) sk[tt] = rsqrtf(s + 1e-6f);
-                else sq[tt] = rsqrtf(s + 1e-6f) * rsqrtf((float)D);
+            for (int tt = 0; tt < CHUNK; ++tt) {
+                const float sum = warp_sum(sq2[tt]);
+                if (lane == 0) wsum[warp][tt] = sum;
             }
         }
         __syncthreads();
-        for (int e = tid; e < n * D; e += NT) {
-            const int tt = e / D, i = e % D;
-            Fq[tt][i] *= sq[tt];
-            Fk[tt][i] *= sk[tt];
+        if (tid < n) {
+            float qs = 0.f, ks = 0.f;
+#pragma unroll
+            for (int w = 0; w < D / 32; ++w) { qs += wsum[w][tid]; ks += wsum[D / 32 + w][tid]; }
+            scal[tid][0] = rsqrtf(qs + 1e-6f) * rsqrtf((float)D);
+            scal[tid][1] = rsqrtf(ks + 1e-6f);
+            scal[tid][2] = expf(decay_h * softplusf_(al + bias_h));
+            scal[tid][3] = sigmoidf_(be);
         }
         __syncthreads();
-        // -------- delta rule: S = a S; u = S k; delta = beta (v - u); S += delta k^T; o = S q
-        for (int tt = 0; tt < n; ++tt) {
-            const float decay = sa[tt], beta = sb[tt];
+        // ---- delta rule over the chunk: S = a S; u = S k; delta = beta (v - u);
+        //      S += delta k^T; o = S q   (k, q normalised through sk, sq)
+#pragma unroll
+        for (int tt = 0; tt < CHUNK; ++tt) {
+            if (tt >= n) break;
+            const float sqn = scal[tt][0], skn = scal[tt][1], decay = scal[tt][2], beta = scal[tt][3];
             const float *kk = Fk[tt], *qq = Fq[tt];
+            float4 k4[NV4];
             float u0 = 0.f, u1 = 0.f;
 #pragma unroll
             for (int i = 0; i < NV4; ++i) {
-                const float4 k4 = *reinterpret_cast<const float4 *>(kk + 16 * i + 4 * j);
+                k4[i] = *reinterpret_cast<const float4 *>(kk + 32 * i + 4 * j);
                 S[4 * i] *= decay; S[4 * i + 1] *= decay; S[4 * i + 2] *= decay; S[4 * i + 3] *= decay;
-                u0 += S[4 * i] * k4.x; u1 += S[4 * i + 1] * k4.y;
-                u0 += S[4 * i + 2] * k4.z; u1 += S[4 * i + 3] * k4.w;
+                u0 += S[4 * i] * k4[i].x; u1 += S[4 * i + 1] * k4[i].y;
+                u0 += S[4 * i + 2] * k4[i].z; u1 += S[4 * i + 3] * k4[i].w;
             }
             float u = u0 + u1;
             u += __shfl_xor_sync(0xffffffffu, u, 1);
             u += __shfl_xor_sync(0xffffffffu, u, 2);
-            const float delta = (Fv[tt][r] - u) * beta;
+            u += __shfl_xor_sync(0xffffffffu, u, 4);
+            const float delta = ((has_row ? Fv[tt][r] : 0.f) - u * skn) * beta * skn;
             float o0 = 0.f, o1 = 0.f;
 #pragma unroll
             for (int i = 0; i < NV4; ++i) {
-                const float4 k4 = *reinterpret_cast<const float4 *>(kk + 16 * i + 4 * j);
-                const float4 q4 = *reinterpret_cast<const float4 *>(qq + 16 * i + 4 * j);
-                S[4 * i] += k4.x * delta; S[4 * i + 1] += k4.y * delta;
-                S[4 * i + 2] += k4.z * delta; S[4 * i + 3] += k4.w * delta;
+                const float4 q4 = *reinterpret_cast<const float4 *>(qq + 32 * i + 4 * j);
+                S[4 * i] += k4[i].x * delta; S[4 * i + 1] += k4[i].y * delta;
+                S[4 * i + 2] += k4[i].z * delta; S[4 * i + 3] += k4[i].w * delta;
                 o0 += S[4 * i] * q4.x; o1 += S[4 * i + 1] * q4.y;
                 o0 += S[4 * i + 2] * q4.z; o1 += S[4 * i + 3] * q4.w;
             }
             float o = o0 + o1;
             o += __shfl_xor_sync(0xffffffffu, o, 1);
             o += __shfl_xor_sync(0xffffffffu, o, 2);
-            if (j == 0) O[tt][r] = o;
+            o += __shfl_xor_sync(0xffffffffu, o, 4);
+            if (j == 0 && has_row) O[tt][r] = o * sqn;
         }
         __syncthreads();
         if (CORE) {
-            for (int e = tid; e < n * ROWS; e += NT) {
-                const int tt = e / ROWS, i = e % ROWS;
-                a.out[((size_t)(t0 + tt) * Hv + h) * D + row0 + i] = O[tt][i];
-            }
+            if (has_out && out_t < n) a.out[((size_t)(t0 + out_t) * Hv + h) * D + row0 + out_i] = O[out_t][out_i];
         } else {
-            // -------- gated RMSNorm over the whole head (cluster-wide sum of squares)
-            float *ps = psum[chunk & 1];
-            for (int tt = warp; tt < n; tt += NW) {
-                float s = 0.f;
-                for (int i = lane; i < ROWS; i += 32) s += O[tt][i] * O[tt][i];
-                s = warp_sum(s);
-                if (lane == 0) ps[tt] = s;
+            // ---- gated RMSNorm over the whole head: warp tt reduces token tt's sum
+            //      of squares over this CTA's rows and pushes it to every rank;
+            //      one thread waits for all partials, the block barrier then
+            //      orders them for the other threads.
+            const int par = chunk & 1;
+            if (warp < CHUNK) {
+                float x = 0.f;
+                for (int i = lane; i < rows; i += 32) x += O[warp][i] * O[warp][i];
+                x = warp_sum(x);
+                if (lane < CPH) {
+                    st_cluster_f32(cluster_map(&osum[par][rank][warp], lane), x);
+                    mbar_arrive_cluster(cluster_map(&osum_bar[par], lane));
+                }
             }
-            if (CPH > 1) cluster.sync(); else __syncthreads();
-            for (int e = tid; e < n * ROWS; e += NT) {
-                const int tt = e / ROWS, i = e % ROWS;
+            if (tid == 0) norm_ok = mbar_wait_cluster(&osum_bar[par], (uint32_t)(chunk >> 1) & 1);
+            __syncthreads();
+            if (norm_ok && has_out && out_t < n) {
                 float total = 0.f;
 #pragma unroll
-                for (int q = 0; q < CPH; ++q)
-                    total += CPH > 1 ? cluster.map_shared_rank(ps, q)[tt] : ps[tt];
+                for (int q = 0; q < CPH; ++q) total += osum[par][q][out_t];
                 const float scale = rsqrtf(total / D + a.eps);
-                const size_t o = ((size_t)(t0 + tt) * Hv + h) * D + row0 + i;
-                a.out[o] = O[tt][i] * scale * a.norm[row0 + i] * siluf_(a.gate[o]);
+                a.out[((size_t)(t0 + out_t) * Hv + h) * D + row0 + out_i] =
+                    O[out_t][out_i] * scale * nw * siluf_(gz);
             }
         }
         __syncthreads();
     }
-    // No CTA may leave while a peer can still read its psum.
-    if (!CORE && CPH > 1) cluster.sync();
 
+    if (has_row) {
 #pragma unroll
-    for (int i = 0; i < NV4; ++i)
-        *reinterpret_cast<float4 *>(srow + 16 * i + 4 * j) =
-            make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
-    // History rows: v channels belong to their rows' CTA; the q/k channels of
-    // key head kh are written by rank 0 of value head kh (h < Hk) only.
-    if (!CORE) {
-#pragma unroll
-        for (int u = 0; u < CPT; ++u) {
-            const int e = tid + u * NT, c = ch[u];
-            if (c < 0 || (e < 2 * D && !(h < Hk && rank == 0))) continue;
-            a.history[c] = h0[u]; a.history[(size_t)C + c] = h1[u]; a.history[2 * (size_t)C + c] = h2[u];
-        }
+        for (int i = 0; i < NV4; ++i)
+            *reinterpret_cast<float4 *>(srow + 32 * i + 4 * j) =
+                make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+    }
+    // History: v channels belong to their rows' CTA; the q/k channels of key
+    // head kh are written by rank 0 of value head kh (h < Hk) only.
+    if (!CORE && c >= 0 && (e >= 2 * D || (h < Hk && rank == 0))) {
+        a.history[c] = h0; a.history[(size_t)C + c] = h1; a.history[2 * (size_t)C + c] = h2;
     }
 }
 
@@ -232,7 +274,7 @@ void check_launch(const char *what) {
 }
 }  // namespace
 
-// D = 128: 4-CTA clusters per value head (32 state rows per CTA); D = 32: one CTA.
+// D = 128: 2-CTA clusters per value head (64 rows each); D = 32: one CTA.
 void delta_run(float *out, float *state, float *history, const float *qkv, const float *gate,
                const float *alpha, const float *beta, const float *conv, const float *decay,
                const float *bias, const float *norm, int T, int Hk, int Hv, int D, float eps,
@@ -241,8 +283,8 @@ void delta_run(float *out, float *state, float *history, const float *qkv, const
     a.out = out; a.state = state; a.history = history; a.qkv = qkv; a.gate = gate;
     a.alpha = alpha; a.beta = beta; a.conv = conv; a.decay = decay; a.bias = bias; a.norm = norm;
     a.T = T; a.Hk = Hk; a.Hv = Hv; a.eps = eps;
-    if (D == 128) delta_kernel<128, 4, false><<<Hv * 4, 128, 0, st>>>(a);
-    else if (D == 32) delta_kernel<32, 1, false><<<Hv, 128, 0, st>>>(a);
+    if (D == 128) delta_kernel<128, 2, false><<<Hv * 2, DeltaShape<128, 2>::NT, 0, st>>>(a);
+    else if (D == 32) delta_kernel<32, 1, false><<<Hv, DeltaShape<32, 1>::NT, 0, st>>>(a);
     else throw std::invalid_argument("unsupported DeltaNet dimension");
     check_launch("delta");
 }
@@ -254,8 +296,8 @@ void delta_core_recurrent(float *out, float *state, const __half *q, const __hal
     a.out = out; a.state = state; a.q16 = q; a.k16 = k; a.v16 = v;
     a.alpha = alpha; a.beta = beta; a.decay = decay; a.bias = bias;
     a.T = T; a.Hk = Hk; a.Hv = Hv;
-    if (D == 128) delta_kernel<128, 4, true><<<Hv * 4, 128, 0, st>>>(a);
-    else if (D == 32) delta_kernel<32, 1, true><<<Hv, 128, 0, st>>>(a);
+    if (D == 128) delta_kernel<128, 2, true><<<Hv * 2, DeltaShape<128, 2>::NT, 0, st>>>(a);
+    else if (D == 32) delta_kernel<32, 1, true><<<Hv, DeltaShape<32, 1>::NT, 0, st>>>(a);
     else throw std::invalid_argument("unsupported DeltaNet dimension");
     check_launch("delta core");
 }
