@@ -35,6 +35,10 @@ H, HKV, HD = 24, 4, 256
 HK, HV, DK = 16, 48, 128
 C = (2 * HK + HV) * DK
 LAYERS = 64
+# DRAM bytes (read + write) of one decode fa_kernel launch at context 139,264,
+# from `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` on
+# `python -m redshift_b200.profile_cases decode 139264` (profiles/fa_kernel_decode_139k.md).
+FA_TRAFFIC_139K = 570674176 + 473088
 
 
 def parse():
@@ -48,6 +52,7 @@ def parse():
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the 32k / prefill side measurements')
+    ap.add_argument('--no-graph', action='store_true', help='launch eagerly instead of replaying a CUDA graph')
     return ap.parse_args()
 
 
@@ -220,6 +225,27 @@ class Step:
             host.copy_(dev, non_blocking=True)
 
 
+def make_events(n, external):
+    import torch
+    return [(torch.cuda.Event(enable_timing=True, external=external),
+             torch.cuda.Event(enable_timing=True, external=external)) for _ in range(n)]
+
+
+def capture(torch, fn):
+    """Capture fn() into a CUDA graph (after one eager call on the capture stream)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
 def bench_b200(args):
     import torch
     rank = int(os.environ.get('RANK', 0))
@@ -241,36 +267,50 @@ def bench_b200(args):
         if dist is not None:
             dist.barrier()
 
+    def max_over_ranks(values):
+        if dist is None:
+            return values
+        t = torch.tensor(values, device='cuda', dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    # One eager step creates the NCCL communicator and every lazy resource.
+    step.run()
+    torch.cuda.synchronize()
+    events = make_events(len(step.attn), external=True)
+    graph, mode = None, 'eager'
+    if not args.no_graph:
+        try:
+            graph = capture(torch, lambda: step.run(events))
+            mode = 'cuda-graph'
+        except Exception as exc:  # capture is an optimisation; report and run eagerly
+            print(f'# CUDA graph capture failed ({exc}); timing eager launches', file=sys.stderr)
+            graph = None
+            events = make_events(len(step.attn), external=False)
+            torch.cuda.synchronize()
+    run_step = graph.replay if graph is not None else (lambda: step.run(events))
+
     for _ in range(args.warmup):
-        step.run()
+        run_step()
     torch.cuda.synchronize()
     if hot.status():
         raise RuntimeError('a kernel reported a timeout during warm-up')
 
     K = args.steps
-    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in step.attn]
-    layer_ms = []
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
         t0.record()
         for _ in range(K):
-            step.run(events)
-            # per-layer event pairs are read back after the region; keep the last step's
-            # pairs plus a running sum through per-step synchronisation-free bookkeeping
-            layer_ms.append(events)
-            events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                      for _ in step.attn]
+            run_step()
         t1.record()
         torch.cuda.synchronize()
         barrier()
     ms = t0.elapsed_time(t1) / K
-    attn_ms = statistics.mean(s.elapsed_time(e) for evs in layer_ms for s, e in evs)
-    if dist is not None:
-        t = torch.tensor([ms, attn_ms], device='cuda')
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, attn_ms = t.tolist()
+    # per-layer attention time of the last timed step (events inside the step)
+    attn_ms = statistics.mean(s.elapsed_time(e) for s, e in events)
+    ms, attn_ms = max_over_ranks([ms, attn_ms])
     if hot.status():
         raise RuntimeError('a kernel reported a timeout during the timed region')
 
@@ -278,31 +318,37 @@ def bench_b200(args):
     e2e = None
     if not args.no_e2e:
         h2d, d2h = step.host_mirror()
+        e2e_graph = None
+        if graph is not None:
+            try:
+                e2e_graph = capture(torch, step.run_e2e)
+            except Exception as exc:
+                print(f'# e2e graph capture failed ({exc}); eager e2e', file=sys.stderr)
+        run_e2e = e2e_graph.replay if e2e_graph is not None else step.run_e2e
         for _ in range(2):
-            step.run_e2e()
+            run_e2e()
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record()
         for _ in range(K):
-            step.run_e2e()
+            run_e2e()
         e1.record()
         torch.cuda.synchronize()
         barrier()
-        e_ms = e0.elapsed_time(e1) / K
-        if dist is not None:
-            t = torch.tensor([e_ms], device='cuda')
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = t.item()
-        e2e = {'value': round(e_ms * 1e3, 2), 'unit': UNIT, 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h}
+        e_ms = max_over_ranks([e0.elapsed_time(e1) / K])[0]
+        e2e = {'value': round(e_ms * 1e3, 2), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
+               'd2h_bytes_per_step': d2h, 'launch': 'cuda-graph' if e2e_graph is not None else 'eager'}
+        del e2e_graph
 
     hbm_peak, tc_peak, peak_kind = peaks()
     kv_rows = step.rows + (args.tokens if step.last else 0)
     attn_bytes = kv_rows * HKV * HD * 2 * 2
     achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
     roofline = {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': hbm_peak, 'unit': 'GB/s',
-                'frac': round(achieved / hbm_peak, 4), 'traffic': None,
+                'frac': round(achieved / hbm_peak, 4),
+                'traffic': FA_TRAFFIC_139K if (args.context == 139264 and world == 1) else None,
                 'kernel': 'attention layer (prepare + split-KV fa_kernel + combine), per rank',
                 'algorithmic_bytes_per_launch': attn_bytes, 'avg_layer_ms': round(attn_ms, 5),
                 'peak_source': peak_kind}
@@ -327,8 +373,9 @@ def bench_b200(args):
                        'delta_layers': 48, 'attention': '24 q / 4 kv heads, d256, fp16 KV',
                        'deltanet': '16 k / 48 v heads, d128, fp32 state',
                        'l2': 'inputs larger than L2 (9.1 GB of KV + 151 MB of state per step)',
-                       'parallelism': f'sequence-split KV x{world} (NCCL all-gather + LSE merge), '
-                                      f'DeltaNet replicated' if world > 1 else 'single GPU'},
+                       'launch': mode,
+                       'parallelism': (f'sequence-split KV x{world} (NCCL all-gather + LSE merge), '
+                                       f'DeltaNet replicated') if world > 1 else 'single GPU'},
             'clocks': clocks.summary(),
             'gpu_launches': step.launches_per_step * K,
             'e2e': e2e,
@@ -339,6 +386,7 @@ def bench_b200(args):
             'extras': extras,
         }
         print(json.dumps(line), flush=True)
+    del graph
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

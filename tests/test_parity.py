@@ -182,3 +182,36 @@ def test_config4_delta_core_against_recurrence(hot):
     out, st = _delta_core_gpu(hot, c, np.zeros((48, 128, 128), np.float32))
     assert rel_err(st, exp_state) <= DELTA_STATE_REL
     close(out, exp_out, 1e-4)
+
+
+# ------------------------------------------------------------------ multi-GPU kernels on one GPU
+@pytest.mark.parametrize('shards,position,batch', [(3, 5000, 8), (2, 139256, 8), (4, 100, 1), (2, 64, 3)])
+def test_sequence_shards_merge_to_the_full_layer(hot, shards, position, batch):
+    """qv_attention_shard over every shard of the plan + qv_attention_merge == qv_attention."""
+    import torch
+    from redshift_b200.sharding import plan, shard_capacity
+    c = I.attention_layer(batch=batch, position=position, seed=4000 + shards)
+    dev = torch.device('cuda')
+    t = lambda k: torch.from_numpy(np.ascontiguousarray(np.asarray(c[k], np.float32))).to(dev)  # noqa: E731
+    qg, key, value, qn, kn = t('q_gate'), t('key'), t('value'), t('q_norm'), t('k_norm')
+    parts = torch.empty((shards, batch, 24, 256), device=dev)
+    lses = torch.empty((shards, batch, 24), device=dev)
+    new_rows = None
+    for g in range(shards):
+        s = plan(position, shards, g, batch)
+        kc = torch.zeros((shard_capacity(s, batch), 4, 256), dtype=torch.float16, device=dev)
+        vc = torch.zeros_like(kc)
+        kc[:s.rows] = torch.from_numpy(c['key_cache'][s.begin:s.begin + s.rows]).to(dev)
+        vc[:s.rows] = torch.from_numpy(c['value_cache'][s.begin:s.begin + s.rows]).to(dev)
+        hot.attention_shard(parts[g], lses[g], kc, vc, s.begin, s.rows, qg, key, value, qn, kn, batch, position)
+        if s.appends:
+            new_rows = (kc[s.rows:].cpu().numpy(), vc[s.rows:].cpu().numpy())
+    out = torch.empty((batch, 24, 256), device=dev)
+    hot.attention_merge(out, parts, lses, shards, batch, qg)
+    assert hot.status() == 0
+    exp_out, exp_k, exp_v = oracle.attention(**c)
+    got = out.cpu().numpy().reshape(-1)
+    assert np.abs(got - exp_out).max() <= ATTN_MAX_ABS
+    close(got, exp_out, 3e-4)
+    close(new_rows[0].astype(np.float64), exp_k[position:].astype(np.float64), 2e-3)
+    assert np.array_equal(new_rows[1], exp_v[position:])
