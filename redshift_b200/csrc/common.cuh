@@ -97,7 +97,7 @@ __device__ __forceinline__ void fence_async_shared() {
 
 // ---------------------------------------------------------------- TMA
 // 2-D tiled bulk tensor load global -> shared, completion via the mbarrier's
-// transaction count.  No multicast.  Coordinates are in elements; the
+// transaction count, into this CTA only.  Coordinates are in elements; the
 // innermost one must be a multiple of 8 for 16-bit data.
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_t *bar,
                                             int x, int y) {
