@@ -12,8 +12,9 @@ microseconds per step (lower is better).
 
 N > 1 runs under torchrun: each rank holds a 1/N sequence shard of every
 attention layer's KV cache, attends over it, and the (partial O, LSE) pairs
-are all-gathered with NCCL and merged (one collective per attention layer);
-DeltaNet layers are replicated.  ``--impl reference`` times the CPU oracle
+are exchanged through peer memory by the library's fused exchange kernel
+(``--nccl-merge``: NCCL all-gather + merge kernel instead) and merged on
+every rank; DeltaNet layers are replicated.  ``--impl reference`` times the CPU oracle
 (the numpy restatement of the reference's cpu_reference.py) on a bounded
 sample of the same step, on rank 0 only.
 """
@@ -41,6 +42,14 @@ LAYERS = 64
 FA_TRAFFIC_139K = 570674176 + 473088
 
 
+RESULT_OUT = sys.stdout
+
+
+def emit(line):
+    RESULT_OUT.write(json.dumps(line) + '\n')
+    RESULT_OUT.flush()
+
+
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
@@ -53,6 +62,7 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the 32k / prefill side measurements')
     ap.add_argument('--no-graph', action='store_true', help='launch eagerly instead of replaying a CUDA graph')
+    ap.add_argument('--nccl-merge', action='store_true', help='N>1: NCCL all-gather instead of the peer exchange')
     return ap.parse_args()
 
 
@@ -160,6 +170,7 @@ class Step:
         self.decay = torch.full((HV,), -1.0, **f32)
         self.bias = torch.zeros(HV, **f32)
         self.norm = torch.ones(DK, **f32)
+        self.exchange = None
         if world > 1:
             need = hot.lib.qv_attention_shard_workspace(tokens, self.rows)
             self.part = torch.empty((tokens, H, HD), **f32)
@@ -169,19 +180,27 @@ class Step:
         else:
             need = hot.lib.qv_attention_workspace(tokens, self.position)
         self.ws = torch.empty(max(int(need), 256), dtype=torch.uint8, device=self.dev)
-        self.launches_per_step = len(self.attn) * (3 if world == 1 else 4) + len(self.delta)
+        self.launches_per_step = len(self.attn) * 3 + len(self.delta)
 
-    def attention_layer(self, a):
+    def use_peer_exchange(self, dist):
+        """Switch the N>1 attention layers to the fused peer-memory exchange."""
+        from redshift_b200.sharding import PeerExchange, plan
+        self.exchange = PeerExchange(self.hot, dist, plan(self.position, self.world, self.rank, self.T))
+
+    def attention_layer(self, a, slot=0):
         hot, T = self.hot, self.T
         if self.world == 1:
             hot.attention(a['out'], a['kc'], a['vc'], a['q_gate'], a['key'], a['value'], self.ones, self.ones,
                           T, self.position, workspace=self.ws)
+        elif self.exchange is not None:
+            self.exchange(a['out'], a['kc'], a['vc'], a['q_gate'], a['key'], a['value'], self.ones, self.ones,
+                          T, self.position, slot, workspace=self.ws)
         else:
             import torch.distributed as dist
             hot.attention_shard(self.part, self.lse, a['kc'], a['vc'], self.begin, self.rows, a['q_gate'],
                                 a['key'], a['value'], self.ones, self.ones, T, self.position, workspace=self.ws)
-            dist.all_gather_into_tensor(self.gpart, self.part)
-            dist.all_gather_into_tensor(self.glse, self.lse)
+            dist.all_gather_into_tensor(self.gpart.view(-1, H, HD), self.part)
+            dist.all_gather_into_tensor(self.glse.view(-1, H), self.lse)
             hot.attention_merge(a['out'], self.gpart, self.glse, self.world, T, a['q_gate'])
 
     def delta_layer(self, d):
@@ -194,7 +213,7 @@ class Step:
             if layer % 4 == 3:
                 if events is not None:
                     events[ai][0].record()
-                self.attention_layer(self.attn[ai])
+                self.attention_layer(self.attn[ai], slot=ai & 1)
                 if events is not None:
                     events[ai][1].record()
                 ai += 1
@@ -261,6 +280,17 @@ def bench_b200(args):
     from redshift_b200 import HotPath
     hot = HotPath()
     step = Step(hot, args.context, args.tokens, rank, world)
+    exchange = 'none'
+    if world > 1:
+        exchange = 'nccl all-gather + merge kernel'
+        if not args.nccl_merge:
+            try:
+                step.use_peer_exchange(dist)
+                exchange = 'fused peer-memory exchange (P2P stores + flags, symmetric memory)'
+            except Exception as exc:
+                print(f'# peer exchange unavailable ({exc}); using NCCL all-gather', file=sys.stderr)
+        if step.exchange is None:       # shard + combine + merge kernels per attention layer
+            step.launches_per_step = len(step.attn) * 4 + len(step.delta)
     torch.cuda.synchronize()
 
     def barrier():
@@ -288,7 +318,13 @@ def bench_b200(args):
             graph = None
             events = make_events(len(step.attn), external=False)
             torch.cuda.synchronize()
-    run_step = graph.replay if graph is not None else (lambda: step.run(events))
+    graphs = [graph] if graph is not None else []      # every graph is reset before teardown
+
+    def run_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step.run(events)
 
     for _ in range(args.warmup):
         run_step()
@@ -322,9 +358,15 @@ def bench_b200(args):
         if graph is not None:
             try:
                 e2e_graph = capture(torch, step.run_e2e)
+                graphs.append(e2e_graph)
             except Exception as exc:
                 print(f'# e2e graph capture failed ({exc}); eager e2e', file=sys.stderr)
-        run_e2e = e2e_graph.replay if e2e_graph is not None else step.run_e2e
+
+        def run_e2e():
+            if e2e_graph is not None:
+                e2e_graph.replay()
+            else:
+                step.run_e2e()
         for _ in range(2):
             run_e2e()
         torch.cuda.synchronize()
@@ -340,7 +382,6 @@ def bench_b200(args):
         e_ms = max_over_ranks([e0.elapsed_time(e1) / K])[0]
         e2e = {'value': round(e_ms * 1e3, 2), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
                'd2h_bytes_per_step': d2h, 'launch': 'cuda-graph' if e2e_graph is not None else 'eager'}
-        del e2e_graph
 
     hbm_peak, tc_peak, peak_kind = peaks()
     kv_rows = step.rows + (args.tokens if step.last else 0)
@@ -373,7 +414,7 @@ def bench_b200(args):
                        'delta_layers': 48, 'attention': '24 q / 4 kv heads, d256, fp16 KV',
                        'deltanet': '16 k / 48 v heads, d128, fp32 state',
                        'l2': 'inputs larger than L2 (9.1 GB of KV + 151 MB of state per step)',
-                       'launch': mode,
+                       'launch': mode, 'exchange': exchange,
                        'parallelism': (f'sequence-split KV x{world} (NCCL all-gather + LSE merge), '
                                        f'DeltaNet replicated') if world > 1 else 'single GPU'},
             'clocks': clocks.summary(),
@@ -385,8 +426,14 @@ def bench_b200(args):
                              'delta_estimate': round((ms - 16 * attn_ms) * 1e3 / 48, 2)},
             'extras': extras,
         }
-        print(json.dumps(line), flush=True)
-    del graph
+        emit(line)
+    # Graphs that captured NCCL calls must be released before the process group.
+    torch.cuda.synchronize()
+    for g in graphs:
+        g.reset()
+    graphs.clear()
+    graph = e2e_graph = None
+    torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -510,11 +557,17 @@ def bench_reference(args):
                                    'DeltaNet layers per step, scaled x16 to the 64-layer step'},
         'e2e': {'value': round(value, 1), 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
     args = parse()
+    # Only the result line goes to stdout: anything libraries print there
+    # (e.g. NCCL's version banner) is sent to stderr instead.
+    global RESULT_OUT
+    sys.stdout.flush()
+    RESULT_OUT = os.fdopen(os.dup(1), 'w')
+    os.dup2(2, 1)
     if args.impl == 'reference':
         bench_reference(args)
     else:

@@ -140,6 +140,26 @@ int qv_attention_shard(float *partial, float *lse, void *key_cache, void *value_
 int qv_attention_merge(float *out, const float *partials, const float *lses, int shards,
                        int batch, const float *q_gate, void *stream);
 
+/* Fused multi-GPU verify: qv_attention_shard, then an all-to-all exchange of
+ * the (partial, LSE) pairs through peer memory and the merge, with no
+ * collective library on the path.  peer_buffers is a device array of `world`
+ * pointers (rank order) to every rank's exchange buffer of
+ * qv_attention_exchange_bytes(world) bytes, zero-initialised before the first
+ * call and mapped into this process (CUDA IPC / symmetric memory).  Each
+ * rank stores its partial into every buffer and raises a flag there, then
+ * waits (bounded; on timeout qv_status reports it) for all ranks' flags.
+ * `slot` (0/1) must alternate between consecutive calls on the same buffers.
+ * All ranks must make the same sequence of calls.  world 1..8, batch 1..10;
+ * out [batch,24,256] is the gated output, identical on every rank. */
+size_t qv_attention_exchange_bytes(int world);
+int qv_attention_shard_exchange(float *out, void *key_cache, void *value_cache,
+                                int shard_begin, int shard_rows,
+                                const float *q_gate, const float *key, const float *value,
+                                const float *q_norm, const float *k_norm,
+                                int batch, int position, float epsilon,
+                                const void *peer_buffers, int world, int rank, int slot,
+                                void *workspace, size_t workspace_bytes, void *stream);
+
 /* Core causal prefill attention (no norm, RoPE or gate), device memory:
  * q [tokens,24,256] fp16 at absolute positions position..position+tokens-1;
  * caches [position+tokens,4,256] fp16; out [tokens,24,256] fp32 =

@@ -476,6 +476,118 @@ attn_combine_kernel(float *out, float *out_lse, const float *part_o, const float
     }
 }
 
+// ---------------------------------------------------------------- fused shard exchange
+// Multi-GPU verify: one kernel per rank combines this shard's split partials
+// of every (token, head) row, stores the normalised partial and its LSE into
+// slot [rank] of every rank's receive buffer (peer memory over NVLink), raises
+// the row's flag there, then waits for all ranks' flags of the rows it owns
+// and merges them (O = sum_g exp(lse_g - LSE) O_g, times sigmoid(gate)).
+// Receive buffer of each rank: data [2 slots][world][EX_ROWS][EX_ROW] floats
+// (256 O, lse, pad) then flags [2 slots][world][EX_ROWS] u32.  `slot`
+// alternates between consecutive calls: a flag is written again only after
+// its consumer has reset it (the sender's next use of the slot comes two
+// calls later, after it has received this rank's partials of the call in
+// between).  Every CTA pushes all its rows before it waits on any, and the
+// grid never exceeds the SM count, so every awaited flag has a running writer.
+constexpr int EX_ROWS = 10 * NQ;                 // rows of the largest decode batch (T <= 10)
+constexpr int EX_ROW = 260;                      // floats per row: 256 O + lse + pad
+constexpr int EX_MAX_WORLD = 8;
+__host__ __device__ constexpr size_t ex_data_floats(int world) { return (size_t)2 * world * EX_ROWS * EX_ROW; }
+__host__ __device__ constexpr size_t ex_bytes(int world) {
+    return ex_data_floats(world) * sizeof(float) + (size_t)2 * world * EX_ROWS * sizeof(uint32_t);
+}
+
+__global__ void __launch_bounds__(256)
+attn_exchange_kernel(float *out, const float *part_o, const float *part_ml, int splits, const float *q_gate,
+                     const uint64_t *peers, int world, int rank, int slot, int T) {
+    const int d = threadIdx.x, rows = T * NQ;
+    __shared__ float wgt[MAX_SPLITS], red[2], den_s, lse_s[EX_MAX_WORLD];
+    __shared__ int ok_s;
+    // ---- phase 1: combine the splits of each owned row and push it to every rank
+    for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+        const int t = row / NQ, h = row % NQ, g = h / GROUP, r = t * GROUP + h % GROUP;
+        const size_t slot0 = (size_t)g * splits * DECODE_ROWS + r;
+        float m = -INFINITY, l = 0.f;
+        if (d < splits) {
+            const float2 ml = *reinterpret_cast<const float2 *>(part_ml + (slot0 + (size_t)d * DECODE_ROWS) * 2);
+            m = ml.x; l = ml.y;
+        }
+        float M = m;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if (d < 64 && (d & 31) == 0) red[d >> 5] = M;
+        __syncthreads();
+        M = fmaxf(red[0], red[1]);
+        const float w = (d < splits && m != -INFINITY) ? exp2f(m - M) : 0.f;
+        if (d < MAX_SPLITS) wgt[d] = w;
+        float den = w * l;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+        __syncthreads();
+        if (d < 64 && (d & 31) == 0) red[d >> 5] = den;
+        __syncthreads();
+        if (d == 0) den_s = red[0] + red[1];
+        __syncthreads();
+        den = den_s;
+        const float *src = part_o + slot0 * HD + d;
+        float v[MAX_SPLITS];
+#pragma unroll
+        for (int e = 0; e < MAX_SPLITS; ++e) v[e] = e < splits ? src[(size_t)e * DECODE_ROWS * HD] : 0.f;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < MAX_SPLITS; ++e) acc[e & 3] += wgt[e] * v[e];
+        const float o = den > 0.f ? ((acc[0] + acc[1]) + (acc[2] + acc[3])) / den : 0.f;
+        const float lse = den > 0.f ? (M + log2f(den)) * 0.6931471805599453f : -INFINITY;
+        for (int q = 0; q < world; ++q) {
+            float *dst = reinterpret_cast<float *>(peers[q]) +
+                         (((size_t)slot * world + rank) * EX_ROWS + row) * EX_ROW;
+            dst[d] = o;
+            if (d == 0) dst[HD] = lse;
+        }
+        __threadfence_system();
+        __syncthreads();
+        if (d < world) {
+            uint32_t *flags = reinterpret_cast<uint32_t *>(reinterpret_cast<float *>(peers[d]) + ex_data_floats(world));
+            st_release_sys(flags + ((size_t)slot * world + rank) * EX_ROWS + row, 1u);
+        }
+        __syncthreads();
+    }
+    // ---- phase 2: wait for every rank's partial of each owned row, merge, reset flags
+    float *mine = reinterpret_cast<float *>(peers[rank]);
+    uint32_t *my_flags = reinterpret_cast<uint32_t *>(mine + ex_data_floats(world));
+    for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+        if (d == 0) ok_s = 1;
+        __syncthreads();
+        if (d < world) {
+            const uint32_t *f = my_flags + ((size_t)slot * world + d) * EX_ROWS + row;
+            const long long t0 = clock64();
+            while (ld_acquire_sys(f) == 0u) {
+                if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok_s = 0; break; }
+            }
+            lse_s[d] = *reinterpret_cast<volatile float *>(mine + (((size_t)slot * world + d) * EX_ROWS + row) * EX_ROW + HD);
+        }
+        __syncthreads();
+        const int t = row / NQ, h = row % NQ;
+        float res = 0.f;
+        if (ok_s) {
+            float M = -INFINITY;
+            for (int q = 0; q < world; ++q) M = fmaxf(M, lse_s[q]);
+            float num = 0.f, den = 0.f;
+            if (M != -INFINITY)
+                for (int q = 0; q < world; ++q) {
+                    if (lse_s[q] == -INFINITY) continue;
+                    const float wq = expf(lse_s[q] - M);
+                    den += wq;
+                    num += wq * mine[(((size_t)slot * world + q) * EX_ROWS + row) * EX_ROW + d];
+                }
+            res = den > 0.f ? num / den : 0.f;
+        }
+        out[((size_t)t * NQ + h) * HD + d] = res * sigmoidf_(q_gate[((size_t)t * NQ + h) * 2 * HD + HD + d]);
+        __syncthreads();
+        if (d < world) my_flags[((size_t)slot * world + d) * EX_ROWS + row] = 0u;
+    }
+}
+
 // Merge per-GPU shard partials (normalised O, natural-log LSE) into the gated
 // output: O = sum_g exp(lse_g - LSE) O_g, times sigmoid(gate).
 __global__ void __launch_bounds__(256)
@@ -611,6 +723,42 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
         launch_fa<true>(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
         check_launch("attention prefill");
     }
+}
+
+size_t attention_exchange_bytes(int world) { return ex_bytes(world); }
+int attention_exchange_max_world() { return EX_MAX_WORLD; }
+
+// Shard attention + fused all-to-all exchange + merge (see attn_exchange_kernel).
+void attention_shard_exchange(float *out, __half *kc, __half *vc, const float *q_gate, const float *key,
+                              const float *value, const float *qn, const float *kn, int T, int position,
+                              int kv_begin, int kv_rows, bool append, float eps, const uint64_t *peers,
+                              int world, int rank, int slot, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (!decode_regime(T)) throw std::invalid_argument("the exchange supports decode batches only");
+    if (world < 1 || world > EX_MAX_WORLD || rank < 0 || rank >= world || (slot != 0 && slot != 1))
+        throw std::invalid_argument("invalid exchange group");
+    if (ws_bytes < attention_workspace_bytes(T, kv_rows)) throw std::invalid_argument("attention workspace too small");
+    configure();
+    uint8_t *w = static_cast<uint8_t *>(ws);
+    const size_t q_bytes = align256((size_t)T * NQ * HD * sizeof(__half));
+    __half *qw = reinterpret_cast<__half *>(w), *qw_lo = reinterpret_cast<__half *>(w + q_bytes);
+    attn_prepare_kernel<<<dim3(T, NQ + NKV), 256, 0, st>>>(q_gate, key, value, qn, kn, qw, qw_lo, kc, vc,
+                                                           position, append ? position - kv_begin : -1, eps);
+    check_launch("attention prepare");
+    const CUtensorMap mk = cache_map(kc, kv_rows), mv = cache_map(vc, kv_rows);
+    FaParams p{};
+    p.q = qw; p.q_lo = qw_lo; p.q_gate = q_gate; p.T = T; p.position = position;
+    p.kv_begin = kv_begin; p.kv_rows = kv_rows;
+    const Split sp = decode_split(kv_rows);
+    p.mode = 0; p.split_tiles = sp.tiles; p.splits = sp.splits; p.direct = 0;
+    p.part_o = reinterpret_cast<float *>(w + 2 * q_bytes);
+    p.part_ml = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(p.part_o) +
+                                          align256((size_t)NKV * sp.splits * DECODE_ROWS * HD * sizeof(float)));
+    launch_fa<true>(mk, mv, p, dim3(sp.splits, NKV), st);
+    check_launch("attention decode");
+    const int grid = min(T * NQ, 144);
+    attn_exchange_kernel<<<grid, 256, 0, st>>>(out, p.part_o, p.part_ml, sp.splits, q_gate, peers, world, rank,
+                                               slot, T);
+    check_launch("attention exchange");
 }
 
 void attention_merge(float *out, const float *parts, const float *lses, int shards, int T,

@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
+#include <stdint.h>
 
 namespace qv {
 
@@ -17,6 +18,12 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
                    size_t ws_bytes, cudaStream_t st);
 void attention_merge(float *out, const float *parts, const float *lses, int shards, int T,
                      const float *q_gate, cudaStream_t st);
+size_t attention_exchange_bytes(int world);
+int attention_exchange_max_world();
+void attention_shard_exchange(float *out, __half *kc, __half *vc, const float *q_gate, const float *key,
+                              const float *value, const float *qn, const float *kn, int T, int position,
+                              int kv_begin, int kv_rows, bool append, float eps, const uint64_t *peers,
+                              int world, int rank, int slot, void *ws, size_t ws_bytes, cudaStream_t st);
 void prefill_core(float *out, float *lse, const __half *q, const __half *kc, const __half *vc, int T,
                   int position, cudaStream_t st);
 

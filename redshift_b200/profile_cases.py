@@ -1,6 +1,7 @@
 """Run one hot-path case a few times, for profilers (ncu) and quick timing.
 
     python -m redshift_b200.profile_cases decode  [context]   # one verify-8 attention layer
+    python -m redshift_b200.profile_cases decode_exchange [context]  # the same through the peer exchange (1 rank)
     python -m redshift_b200.profile_cases delta   [tokens]    # one DeltaNet layer (16/48 heads, d128)
     python -m redshift_b200.profile_cases prefill [tokens]    # core causal prefill attention
     python -m redshift_b200.profile_cases delta_core [tokens] # DeltaNet prefill recurrence (core)
@@ -37,6 +38,27 @@ def make_case(hot, case, size):
         out = torch.empty((T, H, HD), **f32)
         ws = torch.empty(hot.lib.qv_attention_workspace(T, ctx - T), dtype=torch.uint8, device=dev)
         return lambda: hot.attention(out, kc, vc, qg, key, val, ones, ones, T, ctx - T, workspace=ws)
+    if case == 'decode_exchange':
+        # one rank of the fused peer exchange, exchanging with itself (world = 1)
+        T, ctx = 8, size or 139264
+        kc = torch.randn((ctx, HKV, HD), generator=g, device=dev, dtype=torch.float16)
+        vc = torch.randn((ctx, HKV, HD), generator=g, device=dev, dtype=torch.float16)
+        qg = torch.randn((T, H, 2 * HD), generator=g, **f32)
+        key = torch.randn((T, HKV, HD), generator=g, **f32)
+        val = torch.randn((T, HKV, HD), generator=g, **f32)
+        ones = torch.ones(HD, **f32)
+        out = torch.empty((T, H, HD), **f32)
+        ws = torch.empty(hot.lib.qv_attention_shard_workspace(T, ctx - T), dtype=torch.uint8, device=dev)
+        buf = torch.zeros(hot.lib.qv_attention_exchange_bytes(1) // 4, dtype=torch.float32, device=dev)
+        peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
+        state = {'slot': 0}
+
+        def run():
+            hot.attention_shard_exchange(out, kc, vc, 0, ctx - T, qg, key, val, ones, ones, T, ctx - T, peers, 1, 0,
+                                         state['slot'], workspace=ws)
+            state['slot'] ^= 1
+        run.keep = (buf, peers)
+        return run
     if case in ('delta', 'delta_core'):
         T = size or (8 if case == 'delta' else 4096)
         state = torch.randn((HV, DK, DK), generator=g, **f32) * 0.02
@@ -68,7 +90,7 @@ def make_case(hot, case, size):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument('case', choices=['decode', 'delta', 'prefill', 'delta_core'])
+    ap.add_argument('case', choices=['decode', 'decode_exchange', 'delta', 'prefill', 'delta_core'])
     ap.add_argument('size', type=int, nargs='?', default=0)
     ap.add_argument('--reps', type=int, default=3)
     ap.add_argument('--time', action='store_true')

@@ -47,6 +47,8 @@ ADDITIVE_SIGNATURES = {
     'qv_attention_shard_workspace': ([_I, _I], _S),
     'qv_attention_shard': ([_P] * 4 + [_I, _I] + [_P] * 5 + [_I, _I, _F, _P, _S, _P], _I),
     'qv_attention_merge': ([_P] * 3 + [_I, _I, _P, _P], _I),
+    'qv_attention_exchange_bytes': ([_I], _S),
+    'qv_attention_shard_exchange': ([_P] * 3 + [_I, _I] + [_P] * 5 + [_I, _I, _F] + [_P, _I, _I, _I, _P, _S, _P], _I),
     'qv_prefill_attention': ([_P] * 5 + [_I, _I, _P], _I),
     'qv_delta_core': ([_P] * 9 + [_I] * 4 + [_P], _I),
     'qv_status': ([], _I),
@@ -136,6 +138,18 @@ class HotPath:
                                                shard_rows, p(q_gate), p(key), p(value), p(q_norm), p(k_norm),
                                                batch, position, epsilon, p(ws), ws.numel() * ws.element_size(),
                                                self._stream()))
+
+    def attention_shard_exchange(self, out, key_cache, value_cache, shard_begin, shard_rows, q_gate, key, value,
+                                 q_norm, k_norm, batch, position, peers, world, rank, slot, epsilon=1e-6,
+                                 workspace=None):
+        """Shard attention + peer-memory exchange + merge (``peers``: int64 device tensor of buffer addresses)."""
+        need = self.lib.qv_attention_shard_workspace(batch, shard_rows)
+        ws = workspace if workspace is not None else self.workspace(need, out.device)
+        p = self._ptr
+        self.check(self.lib.qv_attention_shard_exchange(
+            p(out), p(key_cache), p(value_cache), shard_begin, shard_rows, p(q_gate), p(key), p(value), p(q_norm),
+            p(k_norm), batch, position, epsilon, p(peers), world, rank, slot, p(ws), ws.numel() * ws.element_size(),
+            self._stream()))
 
     def attention_merge(self, out, partials, lses, shards, batch, q_gate):
         p = self._ptr

@@ -72,3 +72,37 @@ class ShardedAttention:
         self.dist.all_gather_into_tensor(gathered_part.view(-1, *part.shape[1:]), part, group=self.group)
         self.dist.all_gather_into_tensor(gathered_lse.view(-1, *lse.shape[1:]), lse, group=self.group)
         self.hot.attention_merge(out, gathered_part, gathered_lse, s.world, batch, q_gate)
+
+
+class PeerExchange:
+    """Fused multi-GPU verify through peer memory (``qv_attention_shard_exchange``).
+
+    Allocates each rank's exchange buffer in torch symmetric memory (mapped
+    into every rank of ``group``), zeroes it and publishes the rank-ordered
+    array of buffer addresses.  Each call runs the shard's attention, stores
+    its (partial, LSE) into every rank's buffer, raises a flag there, waits for
+    the other ranks' flags and merges; no collective library is on the path.
+    ``slot`` must alternate between consecutive calls (e.g. the attention
+    layer's index parity), the same on every rank.
+    """
+
+    def __init__(self, hot, dist, shard, group=None):
+        import torch
+        import torch.distributed._symmetric_memory as symm_mem
+        self.hot, self.shard = hot, shard
+        nbytes = hot.lib.qv_attention_exchange_bytes(shard.world)
+        if nbytes == 0:
+            raise ValueError('world size not supported by the peer exchange')
+        self.buffer = symm_mem.empty(nbytes // 4, dtype=torch.float32, device='cuda')
+        self.buffer.zero_()
+        self.handle = symm_mem.rendezvous(self.buffer, group if group is not None else dist.group.WORLD)
+        self.peers = torch.tensor(list(self.handle.buffer_ptrs), dtype=torch.int64, device='cuda')
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+
+    def __call__(self, out, key_cache, value_cache, q_gate, key, value, q_norm, k_norm, batch, position, slot,
+                 epsilon=1e-6, workspace=None):
+        s = self.shard
+        self.hot.attention_shard_exchange(out, key_cache, value_cache, s.begin, s.rows, q_gate, key, value, q_norm,
+                                          k_norm, batch, position, self.peers, s.world, s.rank, slot, epsilon,
+                                          workspace=workspace)

@@ -124,3 +124,24 @@ def test_device_entry_points_validate_first(lib):
     assert lib.qv_prefill_attention(v, None, v, v, v, 0, 0, None) == -1
     assert lib.qv_delta(v, v, v, v, v, v, v, v, v, v, v, 1, 16, 48, 64, 1e-6, None) == -1
     assert lib.qv_delta_core(v, v, v, v, v, v, v, v, v, 0, 16, 48, 128, None) == -1
+
+
+def _prototype_arg_counts():
+    text = re.sub(r'/\*.*?\*/', '', HEADER.read_text(), flags=re.S)
+    counts = {}
+    for m in re.finditer(r'\b(qv_[a-z0-9_]+)\s*\(([^)]*)\)\s*;', text):
+        args = m.group(2).strip()
+        counts[m.group(1)] = 0 if args in ('', 'void') else args.count(',') + 1
+    return counts
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every ctypes argtypes list has exactly as many entries as the C prototype."""
+    from redshift_b200.runtime import ADDITIVE_SIGNATURES, MODEL_SIGNATURES, REFERENCE_SIGNATURES
+    counts = _prototype_arg_counts()
+    tables = dict(REFERENCE_SIGNATURES)
+    tables.update(MODEL_SIGNATURES)
+    tables.update({k: v[0] for k, v in ADDITIVE_SIGNATURES.items()})
+    for name, argtypes in tables.items():
+        assert name in counts, name
+        assert len(argtypes) == counts[name], (name, len(argtypes), counts[name])

@@ -215,3 +215,25 @@ def test_sequence_shards_merge_to_the_full_layer(hot, shards, position, batch):
     close(got, exp_out, 3e-4)
     close(new_rows[0].astype(np.float64), exp_k[position:].astype(np.float64), 2e-3)
     assert np.array_equal(new_rows[1], exp_v[position:])
+
+
+def test_peer_exchange_with_a_single_rank_equals_the_layer(hot):
+    """qv_attention_shard_exchange with world=1 (the buffer is this GPU's own) == qv_attention."""
+    import torch
+    c = I.attention_layer(batch=8, position=3000, seed=4100)
+    dev = torch.device('cuda')
+    t = lambda k: torch.from_numpy(np.ascontiguousarray(np.asarray(c[k], np.float32))).to(dev)  # noqa: E731
+    kc = torch.from_numpy(c['key_cache']).to(dev)
+    vc = torch.from_numpy(c['value_cache']).to(dev)
+    nwords = hot.lib.qv_attention_exchange_bytes(1) // 4
+    buf = torch.zeros(nwords, dtype=torch.float32, device=dev)
+    peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
+    exp_out, _, _ = oracle.attention(**c)
+    for slot in (0, 1, 0):           # consecutive calls alternate the slot
+        out = torch.empty((8, 24, 256), device=dev)
+        hot.attention_shard_exchange(out, kc, vc, 0, 3000, t('q_gate'), t('key'), t('value'), t('q_norm'),
+                                     t('k_norm'), 8, 3000, peers, 1, 0, slot)
+        assert hot.status() == 0
+        close(out.cpu().numpy().reshape(-1), exp_out, 3e-4)
+    flags = buf[nwords - 2 * 240:].view(torch.int32)
+    assert int(flags.abs().sum()) == 0, 'consumers reset every flag'
