@@ -179,6 +179,27 @@ int qv_delta_core(float *out, float *state, const void *q, const void *k, const 
                   const float *alpha, const float *beta, const float *decay, const float *bias,
                   int tokens, int key_heads, int value_heads, int dim, void *stream);
 
+/* qv_attention without a workspace argument, for callers that cannot
+ * allocate device memory (no counterpart in the reference ABI).  A serving
+ * runtime that gave all of HBM to its own pools at start-up, or a plugin host
+ * that owns every allocation, can still run the verify/decode attention
+ * layer: the call allocates nothing (no cudaMalloc, no library allocator).
+ * Its scratch space is one fixed 10 MiB array in device memory that each GPU
+ * holds from library load until process exit; that covers batch 1..8 at any
+ * context up to 139264, and larger requests are rejected with an error.
+ * Arguments, layouts and results are those of qv_attention (device pointers,
+ * asynchronous on `stream`), with batch limited to 1..8.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture.  Every call uses the same array and leaves its contents behind;
+ * nothing in it has to start at zero, as each call writes every scratch byte
+ * it reads.  Calls that overlap on the GPU (other streams, other host
+ * threads) race on the array: issue them in order on one stream per device. */
+int qv_attention_noalloc(float *out, void *key_cache, void *value_cache,
+                         const float *q_gate, const float *key, const float *value,
+                         const float *q_norm, const float *k_norm,
+                         int batch, int position, float epsilon, void *stream);
+
 /* Synchronise the current device and return (then clear) the status word
  * that kernels set when a bounded internal wait gives up: 0 = none. */
 int qv_status(void);

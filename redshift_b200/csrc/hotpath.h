@@ -36,6 +36,10 @@ void delta_core_recurrent(float *out, float *state, const __half *q, const __hal
                           const float *alpha, const float *beta, const float *decay, const float *bias,
                           int T, int Hk, int Hv, int D, cudaStream_t st);
 
+// The thread-local message behind qv_error() (runtime.cu).
+void clear_error();
+void record_error(const char *message);
+
 // Device status word (status.cu): 0 = ok, else the first error a kernel raised.
 int read_and_clear_status();
 

@@ -182,6 +182,13 @@ __global__ void rms_norm_kernel(float *out, const float *x, const float *w, int 
 
 }  // namespace
 
+namespace qv {
+// Access to the thread-local message of qv_error() for entry points defined
+// in other files of the library.
+void clear_error() { g_message[0] = '\0'; }
+void record_error(const char *message) { std::snprintf(g_message, sizeof(g_message), "%s", message); }
+}  // namespace qv
+
 extern "C" {
 
 const char *qv_error(void) { return g_message; }

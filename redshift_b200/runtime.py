@@ -52,6 +52,7 @@ ADDITIVE_SIGNATURES = {
     'qv_prefill_attention': ([_P] * 5 + [_I, _I, _P], _I),
     'qv_delta_core': ([_P] * 9 + [_I] * 4 + [_P], _I),
     'qv_status': ([], _I),
+    'qv_attention_noalloc': ([_P] * 8 + [_I, _I, _F, _P], _I),
 }
 
 
