@@ -7,7 +7,10 @@
 // forever on a barrier that is never completed.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <utility>
 
 namespace qv {
 
@@ -100,9 +103,47 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
     return v;
 }
 
+// 64-bit words that carry a value and its ready flag together (low 32 bits:
+// the value's bits, high 32 bits: the flag).  An aligned 64-bit access is
+// single-copy atomic, so a reader that sees the flag also sees the value and
+// no fence is needed between data and flag.
+__device__ __forceinline__ void st_word_sys(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word_sys(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // ---------------------------------------------------------------- proxies
 __device__ __forceinline__ void fence_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Orders this thread's generic-proxy global writes before later async-proxy
+// (TMA) reads of the same memory issued after a CTA-level synchronisation.
+__device__ __forceinline__ void fence_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- launch chaining
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialisation attribute may start while its predecessor in the
+// stream is still running.  grid_dependency_wait() blocks until that
+// predecessor has completed and its memory is visible (a no-op without the
+// attribute); every kernel calls it before touching memory another kernel
+// wrote, and signals its own dependents only after it (so a kernel two
+// launches back has always completed when a kernel starts).
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Named barrier over a subset of the CTA's warps (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
 }
 
 // ---------------------------------------------------------------- TMA
@@ -240,5 +281,26 @@ __device__ __forceinline__ float exp2_approx(float x) {
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x * sigmoidf_(x); }
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+// ---------------------------------------------------------------- host launch
+// Launch `kernel` on `stream` with programmatic stream serialisation: its CTAs
+// may be scheduled (and run up to grid_dependency_wait()) while the previous
+// kernel of the stream drains, which hides the launch gap between the
+// kernels of one layer and between layers.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t stream, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace qv

@@ -87,6 +87,9 @@ delta_kernel(const DeltaArgs a) {
         mbar_init(&osum_bar[1], CPH * CHUNK);
         fence_barrier_init();
     }
+    // State, history and inputs may have been written by the previous kernel.
+    grid_dependency_wait();
+    if (tid == 0) launch_dependents();
 
     // ---- loads that do not depend on the chunk
     float S[COLS];
@@ -268,8 +271,7 @@ delta_kernel(const DeltaArgs a) {
 }
 
 namespace {
-void check_launch(const char *what) {
-    const cudaError_t e = cudaGetLastError();
+void check_launch(cudaError_t e, const char *what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 }  // namespace
@@ -283,10 +285,11 @@ void delta_run(float *out, float *state, float *history, const float *qkv, const
     a.out = out; a.state = state; a.history = history; a.qkv = qkv; a.gate = gate;
     a.alpha = alpha; a.beta = beta; a.conv = conv; a.decay = decay; a.bias = bias; a.norm = norm;
     a.T = T; a.Hk = Hk; a.Hv = Hv; a.eps = eps;
-    if (D == 128) delta_kernel<128, 2, false><<<Hv * 2, DeltaShape<128, 2>::NT, 0, st>>>(a);
-    else if (D == 32) delta_kernel<32, 1, false><<<Hv, DeltaShape<32, 1>::NT, 0, st>>>(a);
+    cudaError_t e;
+    if (D == 128) e = launch_chained(delta_kernel<128, 2, false>, dim3(Hv * 2), dim3(DeltaShape<128, 2>::NT), 0, st, a);
+    else if (D == 32) e = launch_chained(delta_kernel<32, 1, false>, dim3(Hv), dim3(DeltaShape<32, 1>::NT), 0, st, a);
     else throw std::invalid_argument("unsupported DeltaNet dimension");
-    check_launch("delta");
+    check_launch(e, "delta");
 }
 
 void delta_core_recurrent(float *out, float *state, const __half *q, const __half *k, const __half *v,
@@ -296,10 +299,11 @@ void delta_core_recurrent(float *out, float *state, const __half *q, const __hal
     a.out = out; a.state = state; a.q16 = q; a.k16 = k; a.v16 = v;
     a.alpha = alpha; a.beta = beta; a.decay = decay; a.bias = bias;
     a.T = T; a.Hk = Hk; a.Hv = Hv;
-    if (D == 128) delta_kernel<128, 2, true><<<Hv * 2, DeltaShape<128, 2>::NT, 0, st>>>(a);
-    else if (D == 32) delta_kernel<32, 1, true><<<Hv, DeltaShape<32, 1>::NT, 0, st>>>(a);
+    cudaError_t e;
+    if (D == 128) e = launch_chained(delta_kernel<128, 2, true>, dim3(Hv * 2), dim3(DeltaShape<128, 2>::NT), 0, st, a);
+    else if (D == 32) e = launch_chained(delta_kernel<32, 1, true>, dim3(Hv), dim3(DeltaShape<32, 1>::NT), 0, st, a);
     else throw std::invalid_argument("unsupported DeltaNet dimension");
-    check_launch("delta core");
+    check_launch(e, "delta core");
 }
 
 }  // namespace qv

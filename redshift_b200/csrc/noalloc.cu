@@ -21,7 +21,7 @@
 namespace {
 
 // Fixed scratch: large enough for every decode/verify call of up to 8 tokens
-// at any context up to 139,264 (the largest needs 9,971,712 bytes).
+// at any context up to 139,264 (the largest needs 9,775,104 bytes).
 constexpr size_t kScratchBytes = 10u << 20;   // 10 MiB per GPU
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
