@@ -180,7 +180,7 @@ class Step:
         else:
             need = hot.lib.qv_attention_workspace(tokens, self.position)
         self.ws = torch.empty(max(int(need), 256), dtype=torch.uint8, device=self.dev)
-        self.launches_per_step = len(self.attn) * 3 + len(self.delta)
+        self.launches_per_step = len(self.attn) * 2 + len(self.delta)   # fused attention + combine/exchange
 
     def use_peer_exchange(self, dist):
         """Switch the N>1 attention layers to the fused peer-memory exchange."""
@@ -290,7 +290,7 @@ def bench_b200(args):
             except Exception as exc:
                 print(f'# peer exchange unavailable ({exc}); using NCCL all-gather', file=sys.stderr)
         if step.exchange is None:       # shard + combine + merge kernels per attention layer
-            step.launches_per_step = len(step.attn) * 4 + len(step.delta)
+            step.launches_per_step = len(step.attn) * 3 + len(step.delta)   # + shard combine + merge
     torch.cuda.synchronize()
 
     def barrier():
@@ -390,7 +390,8 @@ def bench_b200(args):
     roofline = {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': hbm_peak, 'unit': 'GB/s',
                 'frac': round(achieved / hbm_peak, 4),
                 'traffic': FA_TRAFFIC_139K if (args.context == 139264 and world == 1) else None,
-                'kernel': 'attention layer (prepare + split-KV fa_kernel + combine), per rank',
+                'kernel': 'attention layer (split-KV fa_kernel with fused prepare/append + combine or exchange), '
+                          'per rank',
                 'algorithmic_bytes_per_launch': attn_bytes, 'avg_layer_ms': round(attn_ms, 5),
                 'peak_source': peak_kind}
 
@@ -415,8 +416,8 @@ def bench_b200(args):
                        'deltanet': '16 k / 48 v heads, d128, fp32 state',
                        'l2': 'inputs larger than L2 (9.1 GB of KV + 151 MB of state per step)',
                        'launch': mode, 'exchange': exchange,
-                       'parallelism': (f'sequence-split KV x{world} (NCCL all-gather + LSE merge), '
-                                       f'DeltaNet replicated') if world > 1 else 'single GPU'},
+                       'parallelism': (f'sequence-split KV x{world} ({exchange}), DeltaNet replicated')
+                                      if world > 1 else 'single GPU'},
             'clocks': clocks.summary(),
             'gpu_launches': step.launches_per_step * K,
             'e2e': e2e,

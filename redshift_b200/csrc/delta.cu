@@ -87,6 +87,9 @@ delta_kernel(const DeltaArgs a) {
         mbar_init(&osum_bar[1], CPH * CHUNK);
         fence_barrier_init();
     }
+    // Peers arrive on osum_bar only after it is initialised everywhere (this
+    // needs no memory written by another kernel, so it overlaps the previous one).
+    if (!CORE && CPH > 1) cluster.sync();
     // State, history and inputs may have been written by the previous kernel.
     grid_dependency_wait();
     if (tid == 0) launch_dependents();
@@ -141,8 +144,6 @@ delta_kernel(const DeltaArgs a) {
         gz_n = (!CORE && has_out && out_t < m) ? a.gate[((size_t)(c0 + out_t) * Hv + h) * D + row0 + out_i] : 0.f;
     };
     load_chunk(0);
-    // Peers arrive on osum_bar only after it is initialised everywhere.
-    if (!CORE && CPH > 1) cluster.sync();
 
     for (int t0 = 0, chunk = 0; t0 < a.T; t0 += CHUNK, ++chunk) {
         const int n = min(CHUNK, a.T - t0);
@@ -190,7 +191,8 @@ delta_kernel(const DeltaArgs a) {
         }
         __syncthreads();
         // ---- delta rule over the chunk: S = a S; u = S k; delta = beta (v - u);
-        //      S += delta k^T; o = S q   (k, q normalised through sk, sq)
+        //      S += delta k^T; o = S q   (k, q normalised through sk, sq).  The
+        //      decay is applied inside the update: u = a (S k), S = a S + delta k.
 #pragma unroll
         for (int tt = 0; tt < CHUNK; ++tt) {
             if (tt >= n) break;
@@ -201,7 +203,6 @@ delta_kernel(const DeltaArgs a) {
 #pragma unroll
             for (int i = 0; i < NV4; ++i) {
                 k4[i] = *reinterpret_cast<const float4 *>(kk + 32 * i + 4 * j);
-                S[4 * i] *= decay; S[4 * i + 1] *= decay; S[4 * i + 2] *= decay; S[4 * i + 3] *= decay;
                 u0 += S[4 * i] * k4[i].x; u1 += S[4 * i + 1] * k4[i].y;
                 u0 += S[4 * i + 2] * k4[i].z; u1 += S[4 * i + 3] * k4[i].w;
             }
@@ -209,13 +210,15 @@ delta_kernel(const DeltaArgs a) {
             u += __shfl_xor_sync(0xffffffffu, u, 1);
             u += __shfl_xor_sync(0xffffffffu, u, 2);
             u += __shfl_xor_sync(0xffffffffu, u, 4);
-            const float delta = ((has_row ? Fv[tt][r] : 0.f) - u * skn) * beta * skn;
+            const float delta = ((has_row ? Fv[tt][r] : 0.f) - decay * u * skn) * beta * skn;
             float o0 = 0.f, o1 = 0.f;
 #pragma unroll
             for (int i = 0; i < NV4; ++i) {
                 const float4 q4 = *reinterpret_cast<const float4 *>(qq + 32 * i + 4 * j);
-                S[4 * i] += k4[i].x * delta; S[4 * i + 1] += k4[i].y * delta;
-                S[4 * i + 2] += k4[i].z * delta; S[4 * i + 3] += k4[i].w * delta;
+                S[4 * i] = fmaf(S[4 * i], decay, k4[i].x * delta);
+                S[4 * i + 1] = fmaf(S[4 * i + 1], decay, k4[i].y * delta);
+                S[4 * i + 2] = fmaf(S[4 * i + 2], decay, k4[i].z * delta);
+                S[4 * i + 3] = fmaf(S[4 * i + 3], decay, k4[i].w * delta);
                 o0 += S[4 * i] * q4.x; o1 += S[4 * i + 1] * q4.y;
                 o0 += S[4 * i + 2] * q4.z; o1 += S[4 * i + 3] * q4.w;
             }
