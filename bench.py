@@ -491,14 +491,34 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
     bia = torch.zeros(HV, device='cuda')
     st = torch.zeros((HV, DK, DK), device='cuda')
     od = torch.empty((L, HV, DK), device='cuda')
-    hot.delta_core(od, st, qd, kd, vd, al, be, dec, bia, L, HK, HV, DK)
-    e0.record()
+    ws = torch.empty(hot.lib.qv_delta_chunked_workspace(L, HV), dtype=torch.uint8, device='cuda')
     for _ in range(3):
         st.zero_()
-        hot.delta_core(od, st, qd, kd, vd, al, be, dec, bia, L, HK, HV, DK)
+        hot.delta_chunked(od, st, qd, kd, vd, al, be, dec, bia, L, HK, HV, DK, workspace=ws)
+    t_zero = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_zero[0].record()
+    for _ in range(10):
+        st.zero_()
+    t_zero[1].record()
+    e0.record()
+    for _ in range(10):
+        st.zero_()
+        hot.delta_chunked(od, st, qd, kd, vd, al, be, dec, bia, L, HK, HV, DK, workspace=ws)
     e1.record()
     torch.cuda.synchronize()
-    res['delta_prefill_4096_us'] = round(e0.elapsed_time(e1) / 3 * 1e3, 2)
+    ms = (e0.elapsed_time(e1) - t_zero[0].elapsed_time(t_zero[1])) / 10
+    # chunked WY form per value head and chunk: 10 C^2 D + 6 C D^2 + 2/3 C^3 (C = 64, D = 128)
+    C = 64
+    gdn_flops = (10 * C * C * DK + 6 * C * DK * DK + 2 * C ** 3 / 3) * (L // C) * HV
+    res['delta_prefill_4096_us'] = round(ms * 1e3, 2)
+    res['delta_prefill_tflops'] = round(gdn_flops / (ms * 1e-3) / 1e12, 1)
+    res['delta_prefill_tensor_frac'] = round(gdn_flops / (ms * 1e-3) / 1e12 / tc_peak, 4)
+    e0.record()
+    st.zero_()
+    hot.delta_core(od, st, qd, kd, vd, al, be, dec, bia, L, HK, HV, DK)
+    e1.record()
+    torch.cuda.synchronize()
+    res['delta_prefill_4096_recurrent_us'] = round(e0.elapsed_time(e1) * 1e3, 2)
     return res
 
 

@@ -179,6 +179,19 @@ int qv_delta_core(float *out, float *state, const void *q, const void *k, const 
                   const float *alpha, const float *beta, const float *decay, const float *bias,
                   int tokens, int key_heads, int value_heads, int dim, void *stream);
 
+/* The same computation as qv_delta_core in the chunked form (chunks of 64
+ * tokens, tensor cores): one parallel pass builds every chunk's triangular
+ * (WY) factors, one sequential pass per value head carries the state across
+ * chunks.  dim must be 128.  `workspace` is caller-owned device memory of at
+ * least qv_delta_chunked_workspace(tokens, value_heads) bytes (0 = invalid
+ * arguments); its contents need not be initialised.  Asynchronous on
+ * `stream`. */
+size_t qv_delta_chunked_workspace(int tokens, int value_heads);
+int qv_delta_chunked(float *out, float *state, const void *q, const void *k, const void *v,
+                     const float *alpha, const float *beta, const float *decay, const float *bias,
+                     int tokens, int key_heads, int value_heads, int dim,
+                     void *workspace, size_t workspace_bytes, void *stream);
+
 /* qv_attention without a workspace argument, for callers that cannot
  * allocate device memory (no counterpart in the reference ABI).  A serving
  * runtime that gave all of HBM to its own pools at start-up, or a plugin host

@@ -36,6 +36,13 @@ void delta_core_recurrent(float *out, float *state, const __half *q, const __hal
                           const float *alpha, const float *beta, const float *decay, const float *bias,
                           int T, int Hk, int Hv, int D, cudaStream_t st);
 
+// Chunked gated DeltaNet prefill (gdn_chunk.cu): same inputs / outputs as
+// delta_core_recurrent, D = 128, chunks of 64 tokens on tcgen05.
+size_t delta_chunked_workspace_bytes(int T, int Hv);
+void delta_chunked(float *out, float *state, const __half *q, const __half *k, const __half *v, const float *alpha,
+                   const float *beta, const float *decay, const float *bias, int T, int Hk, int Hv, int D, void *ws,
+                   size_t ws_bytes, cudaStream_t st);
+
 // The thread-local message behind qv_error() (runtime.cu).
 void clear_error();
 void record_error(const char *message);

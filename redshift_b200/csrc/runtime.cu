@@ -420,6 +420,26 @@ int qv_delta_core(float *out, float *state, const void *q, const void *k, const 
     });
 }
 
+size_t qv_delta_chunked_workspace(int tokens, int value_heads) {
+    if (tokens < 1 || tokens > kMaxContext || value_heads < 1 || value_heads > 48) return 0;
+    return qv::delta_chunked_workspace_bytes(tokens, value_heads);
+}
+
+int qv_delta_chunked(float *out, float *state, const void *q, const void *k, const void *v, const float *alpha,
+                     const float *beta, const float *decay, const float *bias, int tokens, int key_heads,
+                     int value_heads, int dim, void *workspace, size_t workspace_bytes, void *stream) {
+    return guarded([&] {
+        require(tokens >= 1 && tokens <= kMaxContext, "tokens must be between 1 and 139264");
+        check_delta_dims(key_heads, value_heads, dim);
+        require(dim == 128, "the chunked DeltaNet path needs dim 128");
+        require(out && state && q && k && v && alpha && beta && decay && bias && workspace, "null DeltaNet buffer");
+        require(workspace_bytes >= qv::delta_chunked_workspace_bytes(tokens, value_heads), "workspace too small");
+        qv::delta_chunked(out, state, static_cast<const __half *>(q), static_cast<const __half *>(k),
+                          static_cast<const __half *>(v), alpha, beta, decay, bias, tokens, key_heads, value_heads,
+                          dim, workspace, workspace_bytes, as_stream(stream));
+    });
+}
+
 int qv_status(void) {
     int status = -1;
     const int rc = guarded([&] {

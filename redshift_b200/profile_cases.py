@@ -5,6 +5,7 @@
     python -m redshift_b200.profile_cases delta   [tokens]    # one DeltaNet layer (16/48 heads, d128)
     python -m redshift_b200.profile_cases prefill [tokens]    # core causal prefill attention
     python -m redshift_b200.profile_cases delta_core [tokens] # DeltaNet prefill recurrence (core)
+    python -m redshift_b200.profile_cases delta_chunked [tokens] # DeltaNet prefill, chunked tcgen05 form
 
 Options: ``--reps N`` launches (default 3), ``--time`` prints the mean
 CUDA-event time of the last N launches.  Inputs are seeded N(0,1) (DeltaNet
@@ -59,7 +60,7 @@ def make_case(hot, case, size):
             state['slot'] ^= 1
         run.keep = (buf, peers)
         return run
-    if case in ('delta', 'delta_core'):
+    if case in ('delta', 'delta_core', 'delta_chunked'):
         T = size or (8 if case == 'delta' else 4096)
         state = torch.randn((HV, DK, DK), generator=g, **f32) * 0.02
         alpha = torch.randn((T, HV), generator=g, **f32)
@@ -77,6 +78,9 @@ def make_case(hot, case, size):
         k = torch.randn((T, HK, DK), generator=g, device=dev, dtype=torch.float16)
         v = torch.randn((T, HV, DK), generator=g, device=dev, dtype=torch.float16)
         out = torch.empty((T, HV, DK), **f32)
+        if case == 'delta_chunked':
+            ws = torch.empty(hot.lib.qv_delta_chunked_workspace(T, HV), dtype=torch.uint8, device=dev)
+            return lambda: hot.delta_chunked(out, state, q, k, v, alpha, beta, decay, bias, T, HK, HV, DK, workspace=ws)
         return lambda: hot.delta_core(out, state, q, k, v, alpha, beta, decay, bias, T, HK, HV, DK)
     if case == 'prefill':
         L = size or 4096
@@ -90,7 +94,7 @@ def make_case(hot, case, size):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument('case', choices=['decode', 'decode_exchange', 'delta', 'prefill', 'delta_core'])
+    ap.add_argument('case', choices=['decode', 'decode_exchange', 'delta', 'prefill', 'delta_core', 'delta_chunked'])
     ap.add_argument('size', type=int, nargs='?', default=0)
     ap.add_argument('--reps', type=int, default=3)
     ap.add_argument('--time', action='store_true')

@@ -51,6 +51,8 @@ ADDITIVE_SIGNATURES = {
     'qv_attention_shard_exchange': ([_P] * 3 + [_I, _I] + [_P] * 5 + [_I, _I, _F] + [_P, _I, _I, _I, _P, _S, _P], _I),
     'qv_prefill_attention': ([_P] * 5 + [_I, _I, _P], _I),
     'qv_delta_core': ([_P] * 9 + [_I] * 4 + [_P], _I),
+    'qv_delta_chunked_workspace': ([_I, _I], _S),
+    'qv_delta_chunked': ([_P] * 9 + [_I] * 4 + [_P, _S, _P], _I),
     'qv_status': ([], _I),
     'qv_attention_noalloc': ([_P] * 8 + [_I, _I, _F, _P], _I),
 }
@@ -174,6 +176,18 @@ class HotPath:
         p = self._ptr
         self.check(self.lib.qv_delta_core(p(out), p(state), p(q), p(k), p(v), p(alpha), p(beta), p(decay),
                                           p(bias), tokens, key_heads, value_heads, dim, self._stream()))
+
+    def delta_chunked(self, out, state, q, k, v, alpha, beta, decay, bias, tokens, key_heads, value_heads, dim,
+                      workspace=None):
+        """qv_delta_chunked; allocates the workspace when none is given."""
+        p = self._ptr
+        need = self.lib.qv_delta_chunked_workspace(tokens, value_heads)
+        if workspace is None:
+            import torch
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=out.device)
+        self.check(self.lib.qv_delta_chunked(p(out), p(state), p(q), p(k), p(v), p(alpha), p(beta), p(decay),
+                                             p(bias), tokens, key_heads, value_heads, dim, p(workspace),
+                                             workspace.numel() * workspace.element_size(), self._stream()))
 
     def status(self):
         """Synchronise and return the kernel status word (0 = no timeout)."""

@@ -124,6 +124,12 @@ def test_device_entry_points_validate_first(lib):
     assert lib.qv_prefill_attention(v, None, v, v, v, 0, 0, None) == -1
     assert lib.qv_delta(v, v, v, v, v, v, v, v, v, v, v, 1, 16, 48, 64, 1e-6, None) == -1
     assert lib.qv_delta_core(v, v, v, v, v, v, v, v, v, 0, 16, 48, 128, None) == -1
+    assert lib.qv_delta_chunked_workspace(0, 48) == 0
+    assert lib.qv_delta_chunked_workspace(4096, 48) > 0
+    need = lib.qv_delta_chunked_workspace(64, 48)
+    assert lib.qv_delta_chunked(v, v, v, v, v, v, v, v, v, 64, 16, 48, 32, v, need, None) == -1   # dim 32
+    assert lib.qv_delta_chunked(v, v, v, v, v, v, v, v, v, 64, 16, 48, 128, v, need - 1, None) == -1
+    assert lib.qv_delta_chunked(v, v, v, v, v, v, v, v, v, 64, 16, 48, 128, None, need, None) == -1
 
 
 def _prototype_arg_counts():

@@ -175,6 +175,62 @@ def _delta_core_gpu(hot, c, state):
     return out.cpu().numpy(), st.cpu().numpy()
 
 
+def _delta_chunked_gpu(hot, c, state):
+    import torch
+    dev = torch.device('cuda')
+    L, hk, d = c['q'].shape
+    hv = c['v'].shape[1]
+    t16 = lambda a: torch.from_numpy(a.view(np.uint16).copy()).to(dev).view(torch.float16)  # noqa: E731
+    t32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)  # noqa: E731
+    st = t32(state)
+    out = torch.empty((L, hv, d), dtype=torch.float32, device=dev)
+    hot.delta_chunked(out, st, t16(c['q']), t16(c['k']), t16(c['v']), t32(c['alpha']), t32(c['beta']),
+                      t32(np.full(hv, -1.0)), t32(np.zeros(hv)), L, hk, hv, d)
+    assert hot.status() == 0
+    return out.cpu().numpy(), st.cpu().numpy()
+
+
+@pytest.mark.parametrize('length,with_state', [(1, False), (64, False), (65, True), (200, True), (512, False)])
+def test_chunked_delta_against_recurrence(hot, length, with_state):
+    """qv_delta_chunked (chunks of 64 on tensor cores) == the fp64 token recurrence:
+    a single token, exactly one chunk, a ragged last chunk, a non-zero initial state."""
+    c = I.delta_prefill(length=length, seed=7000 + length)
+    q, k, g, b = oracle.hotpath.prepare_delta_inputs(c['q'], c['k'], c['alpha'], c['beta'])
+    s0 = (np.random.default_rng(length).standard_normal((48, 128, 128)) * 0.02 if with_state
+          else np.zeros((48, 128, 128)))
+    exp_out, exp_state = oracle.delta_core(s0, q, k, c['v'], g, b)
+    out, st = _delta_chunked_gpu(hot, c, s0.astype(np.float32))
+    assert rel_err(st, exp_state) <= DELTA_STATE_REL
+    close(out, exp_out, 1e-4)
+
+
+def test_config4_chunked_prefill_then_verify(hot):
+    """Config 4 end to end: a 4,096-token chunked prefill from a zero state, its state handed to 8
+    recurrent verify tokens, checked against the token-by-token CPU recurrence over all 4,104 tokens
+    (value heads 0-15, which use key heads 0-15), and all 48 heads against the recurrent kernel."""
+    import torch
+    L = 4096
+    c = I.delta_prefill(length=L + 8)
+    pre = {k: v[:L] for k, v in c.items()}
+    ver = {k: v[L:] for k, v in c.items()}
+    out_c, st_c = _delta_chunked_gpu(hot, pre, np.zeros((48, 128, 128), np.float32))
+    out_r, st_r = _delta_core_gpu(hot, pre, np.zeros((48, 128, 128), np.float32))
+    assert rel_err(st_c, st_r) <= DELTA_STATE_REL
+    close(out_c, out_r, 1e-4)
+    out_v, st_v = _delta_core_gpu(hot, ver, st_c)
+    q, k, g, b = oracle.hotpath.prepare_delta_inputs(c['q'], c['k'], c['alpha'], c['beta'])
+    heads = 16
+    exp_pre, exp_state = oracle.delta_core(np.zeros((heads, 128, 128)), q[:L], k[:L], c['v'][:L, :heads],
+                                           g[:L, :heads], b[:L, :heads])
+    exp_ver, exp_final = oracle.delta_core(exp_state, q[L:], k[L:], c['v'][L:, :heads], g[L:, :heads],
+                                           b[L:, :heads])
+    assert rel_err(st_c[:heads], exp_state) <= DELTA_STATE_REL
+    assert rel_err(st_v[:heads], exp_final) <= DELTA_STATE_REL
+    close(out_c[:, :heads], exp_pre, 1e-4)
+    close(out_v[:, :heads], exp_ver, 1e-4)
+    del torch
+
+
 def test_config4_delta_core_against_recurrence(hot):
     c = I.delta_prefill(length=512)
     q, k, g, b = oracle.hotpath.prepare_delta_inputs(c['q'], c['k'], c['alpha'], c['beta'])
