@@ -41,6 +41,7 @@
 #include <cudaTypedefs.h>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 
 namespace qv {
 
@@ -74,8 +75,9 @@ __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
 // ------------------------------------------------------------------ prep
 constexpr int PREP_SA = 0;                       // A: [2 blocks][128 rows][128 B] (K^ rows 0-63, Q^ rows 64-127)
 constexpr int PREP_SB = 32768;                   // B: [2 blocks][64 rows][128 B] (K^)
-constexpr int PREP_BM = 49152;                   // fp32 [64][65]
-constexpr int PREP_SMALL = PREP_BM + 64 * 65 * 4;
+constexpr int PREP_BM = 49152;                   // fp32 [64][BMS]
+constexpr int BMS = 68;                          // row stride: 16-byte rows, conflict-free row stores
+constexpr int PREP_SMALL = PREP_BM + 64 * BMS * 4;
 constexpr int PREP_SMEM = PREP_SMALL + 4 * 64 * 4 + 64;
 
 __global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
@@ -86,6 +88,7 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
     }
     uint8_t *sa = smem + PREP_SA, *sb = smem + PREP_SB;
     float *bm = reinterpret_cast<float *>(smem + PREP_BM);
+    // log2-scaled cumulative log decay, beta, 1/|k|, 1/(|q| sqrt D)
     float *gam = reinterpret_cast<float *>(smem + PREP_SMALL), *bet = gam + 64, *ik = bet + 64, *iq = ik + 64;
     uint64_t *bar = reinterpret_cast<uint64_t *>(iq + 64);
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 1);
@@ -98,29 +101,55 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
     grid_dependency_wait();
     if (tid == 0) launch_dependents();
 
-    // (1) normalised keys / queries as fp16 MMA operands
-    for (int i = 0; i < 16; ++i) {
-        const int t = warp * 16 + i;
-        uint2 kr = make_uint2(0, 0), qr = make_uint2(0, 0);
-        if (t < n) {
-            kr = *reinterpret_cast<const uint2 *>(p.k + ((size_t)(t0 + t) * p.Hk + kh) * GD + 4 * lane);
-            qr = *reinterpret_cast<const uint2 *>(p.q + ((size_t)(t0 + t) * p.Hk + kh) * GD + 4 * lane);
+    // (1) normalised keys / queries as fp16 MMA operands: warp w takes tokens
+    //     16w..16w+15, lane l dims [4l, 4l+4); the 32 sums reduce together.
+    {
+        uint2 kr[16], qr[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int t = warp * 16 + i;
+            kr[i] = qr[i] = make_uint2(0, 0);
+            if (t < n) {
+                kr[i] = *reinterpret_cast<const uint2 *>(p.k + ((size_t)(t0 + t) * p.Hk + kh) * GD + 4 * lane);
+                qr[i] = *reinterpret_cast<const uint2 *>(p.q + ((size_t)(t0 + t) * p.Hk + kh) * GD + 4 * lane);
+            }
         }
-        const float2 k01 = __half22float2(*reinterpret_cast<__half2 *>(&kr.x));
-        const float2 k23 = __half22float2(*reinterpret_cast<__half2 *>(&kr.y));
-        const float2 q01 = __half22float2(*reinterpret_cast<__half2 *>(&qr.x));
-        const float2 q23 = __half22float2(*reinterpret_cast<__half2 *>(&qr.y));
-        const float sk = warp_sum(k01.x * k01.x + k01.y * k01.y + k23.x * k23.x + k23.y * k23.y);
-        const float sq = warp_sum(q01.x * q01.x + q01.y * q01.y + q23.x * q23.x + q23.y * q23.y);
-        const float rk = rsqrtf(sk + 1e-6f), rq = rsqrtf(sq + 1e-6f) * rsqrtf((float)GD);
-        if (lane == 0) { ik[t] = rk; iq[t] = rq; }
-        const uint2 kn = pack4(k01.x * rk, k01.y * rk, k23.x * rk, k23.y * rk);
-        const uint2 qn = pack4(q01.x * rq, q01.y * rq, q23.x * rq, q23.y * rq);
-        *reinterpret_cast<uint2 *>(sa + sw_off(128, t, 4 * lane)) = kn;
-        *reinterpret_cast<uint2 *>(sa + sw_off(128, 64 + t, 4 * lane)) = qn;
-        *reinterpret_cast<uint2 *>(sb + sw_off(64, t, 4 * lane)) = kn;
+        float sk[16], sq[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float2 a = __half22float2(*reinterpret_cast<__half2 *>(&kr[i].x));
+            const float2 b = __half22float2(*reinterpret_cast<__half2 *>(&kr[i].y));
+            const float2 e = __half22float2(*reinterpret_cast<__half2 *>(&qr[i].x));
+            const float2 f = __half22float2(*reinterpret_cast<__half2 *>(&qr[i].y));
+            sk[i] = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+            sq[i] = e.x * e.x + e.y * e.y + f.x * f.x + f.y * f.y;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                sk[i] += __shfl_xor_sync(0xffffffffu, sk[i], o);
+                sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], o);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int t = warp * 16 + i;
+            const float rk = rsqrtf(sk[i] + 1e-6f), rq = rsqrtf(sq[i] + 1e-6f) * rsqrtf((float)GD);
+            if (lane == 0) { ik[t] = rk; iq[t] = rq; }
+            const float2 a = __half22float2(*reinterpret_cast<__half2 *>(&kr[i].x));
+            const float2 b = __half22float2(*reinterpret_cast<__half2 *>(&kr[i].y));
+            const float2 e = __half22float2(*reinterpret_cast<__half2 *>(&qr[i].x));
+            const float2 f = __half22float2(*reinterpret_cast<__half2 *>(&qr[i].y));
+            const uint2 kn = pack4(a.x * rk, a.y * rk, b.x * rk, b.y * rk);
+            const uint2 qn = pack4(e.x * rq, e.y * rq, f.x * rq, f.y * rq);
+            *reinterpret_cast<uint2 *>(sa + sw_off(128, t, 4 * lane)) = kn;
+            *reinterpret_cast<uint2 *>(sa + sw_off(128, 64 + t, 4 * lane)) = qn;
+            *reinterpret_cast<uint2 *>(sb + sw_off(64, t, 4 * lane)) = kn;
+        }
     }
-    // (2) log decays, their inclusive prefix sum over the chunk, and beta
+    // (2) log decays, their inclusive prefix sum over the chunk (log2 units),
+    //     and beta
     if (warp == 0) {
         float g[2], b[2];
         const float dh = p.decay[h], bh = p.bias[h];
@@ -130,7 +159,7 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
             g[e] = 0.f; b[e] = 0.f;
             if (t < n) {
                 const size_t idx = (size_t)(t0 + t) * p.Hv + h;
-                g[e] = dh * softplusf_(p.alpha[idx] + bh);
+                g[e] = dh * softplusf_(p.alpha[idx] + bh) * 1.4426950408889634f;
                 b[e] = sigmoidf_(p.beta[idx]);
             }
         }
@@ -160,67 +189,89 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
                        sw128_desc(b0 + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024), idesc, k > 0 ? 1u : 0u);
         mma_commit(bar);
     }
-    const bool ok = mbar_wait(bar, 0, abort_flag);
+    mbar_wait(bar, 0, abort_flag);
     tc_fence_after();
-    // (4) row tid of the product: B (tid < 64) or Mq (tid >= 64)
-    float x[64];
+    // (4) row tid of the product: B = beta_t G(t,s) k^_t.k^_s, s < t (tid < 64)
+    //     or Mq = G(t,s) q^_t.k^_s, s <= t (tid >= 64); G(t,s) = 2^(gam_t - gam_s).
+    {
+        float x[64];
 #pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + q4 * 16, *reinterpret_cast<float(*)[16]>(x + q4 * 16));
-    tmem_wait_ld();
-    const size_t unit = (size_t)h * p.nch + c;
-    if (tid < 64) {
-        const int t = tid;
-        const float gt = gam[t], bt = bet[t];
+        for (int q4 = 0; q4 < 4; ++q4)
+            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + q4 * 16, *reinterpret_cast<float(*)[16]>(x + q4 * 16));
+        tmem_wait_ld();
+        const size_t unit = (size_t)h * p.nch + c;
+        if (tid < 64) {
+            const int t = tid;
+            const float gt = gam[t], bt = bet[t];
 #pragma unroll
-        for (int s = 0; s < 64; ++s) bm[t * 65 + s] = s < t ? bt * expf(gt - gam[s]) * x[s] : 0.f;
-    } else {
-        const int t = tid - 64;
-        const float gt = gam[t];
-        uint4 *dst = reinterpret_cast<uint4 *>(p.mq + (unit * GC + t) * GC);
-#pragma unroll
-        for (int s8 = 0; s8 < 8; ++s8) {
-            float m[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int s = s8 * 8 + e;
-                m[e] = s <= t ? expf(gt - gam[s]) * x[s] : 0.f;
+            for (int s4 = 0; s4 < 64; s4 += 4) {
+                float4 v;
+                v.x = s4 < t ? bt * exp2_approx(gt - gam[s4]) * x[s4] : 0.f;
+                v.y = s4 + 1 < t ? bt * exp2_approx(gt - gam[s4 + 1]) * x[s4 + 1] : 0.f;
+                v.z = s4 + 2 < t ? bt * exp2_approx(gt - gam[s4 + 2]) * x[s4 + 2] : 0.f;
+                v.w = s4 + 3 < t ? bt * exp2_approx(gt - gam[s4 + 3]) * x[s4 + 3] : 0.f;
+                *reinterpret_cast<float4 *>(bm + t * BMS + s4) = v;
             }
-            const uint2 lo = pack4(m[0], m[1], m[2], m[3]), hi = pack4(m[4], m[5], m[6], m[7]);
-            dst[s8] = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        } else {
+            const int t = tid - 64;
+            const float gt = gam[t];
+            uint4 *dst = reinterpret_cast<uint4 *>(p.mq + (unit * GC + t) * GC);
+#pragma unroll
+            for (int s8 = 0; s8 < 8; ++s8) {
+                float m[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int s = s8 * 8 + e;
+                    m[e] = s <= t ? exp2_approx(gt - gam[s]) * x[s] : 0.f;
+                }
+                const uint2 lo = pack4(m[0], m[1], m[2], m[3]), hi = pack4(m[4], m[5], m[6], m[7]);
+                dst[s8] = make_uint4(lo.x, lo.y, hi.x, hi.y);
+            }
         }
     }
     __syncthreads();
 
-    // (5) X = (I + B)^-1 by forward substitution: thread pair (j, par) owns
-    //     column j, par splits the dot products (even / odd s).
-    const int j = tid >> 1, par = tid & 1;
-    float xc[64];
+    // (5) X = (I + B)^-1 (unit lower triangular) by forward substitution, one
+    //     thread per column j (warps 0 and 1); column j is zero above row j,
+    //     so warp 1 (j >= 32) starts at row 32.  (6) The owner of column j then
+    //     writes row j of T^T, T = X diag(beta), as fp16 hi + lo, and of
+    //     (T diag(g / |k|))^T as fp16.  (7) Warps 2-3 write the per-token scales
+    //     {g_t / (|q_t| sqrt D), (g_C / g_t) / |k_t|, g_C, 0}.
+    const size_t unit = (size_t)h * p.nch + c;
+    auto solve_and_store = [&](auto first_row) {
+        constexpr int R0 = decltype(first_row)::value;
+        const int j = tid;
+        float xv[64];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-        float acc = 0.f;
+        for (int i = 0; i < R0; ++i) xv[i] = 0.f;
 #pragma unroll
-        for (int s = 0; s < i; ++s)
-            if ((s & 1) == par) acc += bm[i * 65 + s] * xc[s];
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        xc[i] = (i == j ? 1.f : 0.f) - acc;
-    }
-    // (6) T = X diag(beta) and T diag(g / |k|), stored transposed (row j of
-    //     T^T = column j of T), half a row per thread.
-    {
-        const float bj = bet[j], wj = bj * expf(gam[j]) * ik[j];
-        const size_t row = (unit * GC + j) * GC + 32 * par;
+        for (int i = R0; i < 64; ++i) {
+            float a0 = 0.f, a1 = 0.f;
+            const float *brow = bm + i * BMS;
+#pragma unroll
+            for (int s4 = R0; s4 < (i & ~3); s4 += 4) {
+                const float4 b4 = *reinterpret_cast<const float4 *>(brow + s4);
+                a0 += b4.x * xv[s4]; a1 += b4.y * xv[s4 + 1];
+                a0 += b4.z * xv[s4 + 2]; a1 += b4.w * xv[s4 + 3];
+            }
+#pragma unroll
+            for (int s = (i & ~3) > R0 ? (i & ~3) : R0; s < i; ++s) a0 += brow[s] * xv[s];
+            xv[i] = (i == j ? 1.f : 0.f) - (a0 + a1);
+        }
+        const float bj = bet[j], wj = bj * exp2f(gam[j]) * ik[j];
+        const size_t row = (unit * GC + j) * GC;
         uint4 *ph = reinterpret_cast<uint4 *>(p.tt_hi + row), *pl = reinterpret_cast<uint4 *>(p.tt_lo + row);
         uint4 *pp = reinterpret_cast<uint4 *>(p.ttp + row);
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
+        for (int q8 = 0; q8 < 8; ++q8) {
             float hv[8], lv[8], pv[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-                const float xv = par ? xc[32 + q8 * 8 + e] : xc[q8 * 8 + e];     // compile-time indices
-                const float v = xv * bj;
+                const float xe = xv[q8 * 8 + e];
+                const float v = xe * bj;
                 const float hh = __half2float(__float2half_rn(v));
                 hv[e] = hh; lv[e] = v - hh;
-                pv[e] = xv * wj;
+                pv[e] = xe * wj;
             }
             uint2 a = pack4(hv[0], hv[1], hv[2], hv[3]), b = pack4(hv[4], hv[5], hv[6], hv[7]);
             ph[q8] = make_uint4(a.x, a.y, b.x, b.y);
@@ -229,16 +280,16 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
             a = pack4(pv[0], pv[1], pv[2], pv[3]); b = pack4(pv[4], pv[5], pv[6], pv[7]);
             pp[q8] = make_uint4(a.x, a.y, b.x, b.y);
         }
-    }
-    // (7) per-token scales: {g_t / (|q_t| sqrt D), (g_C / g_t) / |k_t|, g_C, 0}
-    if (tid < 64) {
-        const int t = tid;
+    };
+    if (warp == 0) solve_and_store(std::integral_constant<int, 0>{});
+    else if (warp == 1) solve_and_store(std::integral_constant<int, 32>{});
+    else if (tid >= 64) {
+        const int t = tid - 64;
         const float gl = gam[n - 1];
-        const float4 v = t < n ? make_float4(expf(gam[t]) * iq[t], expf(gl - gam[t]) * ik[t], expf(gl), 0.f)
-                               : make_float4(0.f, 0.f, expf(gl), 0.f);
+        const float4 v = t < n ? make_float4(exp2f(gam[t]) * iq[t], exp2f(gl - gam[t]) * ik[t], exp2f(gl), 0.f)
+                               : make_float4(0.f, 0.f, exp2f(gl), 0.f);
         reinterpret_cast<float4 *>(p.sc)[unit * GC + t] = v;
     }
-    (void)ok;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -286,7 +337,7 @@ gdn_scan_kernel(const __grid_constant__ CUtensorMap mTh, const __grid_constant__
         return;
     }
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SCAN_BAR);
-    uint64_t *full = bars, *bm1 = bars + 2, *bm3 = bars + 3, *bm5 = bars + 4;
+    uint64_t *full = bars, *bm1 = bars + 2, *bm3 = bars + 3, *bm5 = bars + 4, *bm4 = bars + 5;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 6);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 7);
     const int half = blockIdx.x, h = blockIdx.y, kh = h % p.Hk;
@@ -297,7 +348,7 @@ gdn_scan_kernel(const __grid_constant__ CUtensorMap mTh, const __grid_constant__
 
     if (tid == 0) {
         mbar_init(full, 1); mbar_init(full + 1, 1);
-        mbar_init(bm1, 1); mbar_init(bm3, 1); mbar_init(bm5, 1);
+        mbar_init(bm1, 1); mbar_init(bm3, 1); mbar_init(bm4, 1); mbar_init(bm5, 1);
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tmap(&mTh); prefetch_tmap(&mTl); prefetch_tmap(&mTp); prefetch_tmap(&mMq);
@@ -327,11 +378,19 @@ gdn_scan_kernel(const __grid_constant__ CUtensorMap mTh, const __grid_constant__
         tma2(b + SB_V, &mV, f, h * GD + half * 64, c * GC);
         tma2(b + SB_SC, &mSc, f, 0, unit_row);
     };
-    if (tid == 0) issue_loads(0);
+    int last_issued = min(p.nch, 2) - 1;          // (thread 0) latest chunk whose loads are in flight
+    if (tid == 0) {
+        issue_loads(0);
+        if (p.nch > 1) issue_loads(1);
+    }
+    uint8_t *sh = smem + SCAN_SH, *nw = smem + SCAN_NW, *dl = smem + SCAN_DL;
+    uint8_t *dhi = smem + SCAN_DH, *dlo = smem + SCAN_DLO;
+    const uint32_t sh_a = smem_addr(sh), nw_a = smem_addr(nw), dl_a = smem_addr(dl);
+    const uint32_t dh_a = smem_addr(dhi), dlo_a = smem_addr(dlo);
+    auto buf_of = [&](int c) { return smem + SCAN_BUF + (c & 1) * 75776; };
 
-    // Initial state rows (value dims half*64 + row) into TMEM (fp32) and the
-    // fp16 operand image (K-major [64][128]); this thread covers 64 columns.
-    uint8_t *sh = smem + SCAN_SH;
+    // Initial state rows (value dims half*64 + row) into TMEM, fp32; this
+    // thread covers 64 columns.
     float *srow = p.state + ((size_t)h * GD + half * 64 + row) * GD + side * 64;
 #pragma unroll
     for (int q4 = 0; q4 < 4; ++q4) {
@@ -342,173 +401,214 @@ gdn_scan_kernel(const __grid_constant__ CUtensorMap mTh, const __grid_constant__
             v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
         }
         tmem_st16(tmem + tq + TS + side * 64 + q4 * 16, v);
-        if (holds) {
-#pragma unroll
-            for (int e = 0; e < 16; e += 4)
-                *reinterpret_cast<uint2 *>(sh + sw_off(64, row, side * 64 + q4 * 16 + e)) =
-                    pack4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-        }
     }
     tmem_wait_st();
-    fence_async_shared();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
 
-    const uint32_t sh_a = smem_addr(sh), nw_a = smem_addr(smem + SCAN_NW), dl_a = smem_addr(smem + SCAN_DL);
-    const uint32_t dh_a = smem_addr(smem + SCAN_DH), dlo_a = smem_addr(smem + SCAN_DLO);
-    uint8_t *nw = smem + SCAN_NW, *dl = smem + SCAN_DL, *dhi = smem + SCAN_DH, *dlo = smem + SCAN_DLO;
-    for (int c = 0; c < p.nch; ++c) {
-        const int b = c & 1;
-        uint8_t *buf = smem + SCAN_BUF + b * 75776;
-        const uint32_t ba = smem_addr(buf);
-        if (tid == 0 && c + 1 < p.nch) issue_loads(c + 1);
-        mbar_wait(full + b, (uint32_t)(c >> 1) & 1, abort_flag);
-        // ---- U = T V, W = T diag(g/|k|) K, O1 = Q S^T
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t i_u = idesc_f16(64, 64, true, true), i_w = idesc_f16(64, 128, true, true);
-            const uint32_t i_o = idesc_f16(64, 64, false, false);
+    // U = T V and W = T diag(g/|k|) K of chunk c (independent of the state).
+    // Shared-memory descriptors are formed once per operand base; a K step
+    // adds its byte offset / 16 to the start-address field (every address
+    // here is below 256 KB, so the 14-bit field never carries).
+    auto kmaj = [](uint32_t a) { return sw128_desc(a, 16, 1024); };
+    auto mnmaj = [](uint32_t a) { return sw128_desc(a, TILE, 1024); };
+    auto koff = [](int k) { return (uint64_t)((k >> 2) * (TILE >> 4) + (k & 3) * 2); };   // K-major, K = 16 k
+    auto moff = [](int k) { return (uint64_t)(k * 128); };                                // MN-major, K = 16 k
+    const uint64_t d_sh = kmaj(sh_a), d_nw = kmaj(nw_a), d_dl = mnmaj(dl_a), d_dh = mnmaj(dh_a), d_dlo = mnmaj(dlo_a);
+    const uint32_t i_u = idesc_f16(64, 64, true, true), i_w = idesc_f16(64, 128, true, true);
+    const uint32_t i_d = idesc_f16(64, 64, false, false), i_m = idesc_f16(64, 64, false, true);
+    const uint32_t i_s = idesc_f16(64, 128, true, true);
+    auto issue_uw = [&](int c) {
+        const uint32_t ba = smem_addr(buf_of(c));
+        const uint64_t th = mnmaj(ba + SB_TH), tl = mnmaj(ba + SB_TL), tp = mnmaj(ba + SB_TP);
+        const uint64_t dv = mnmaj(ba + SB_V), dk = mnmaj(ba + SB_K);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                mma_f16_ss(tmem + TU, sw128_desc(ba + SB_TH + k * 2048, TILE, 1024),
-                           sw128_desc(ba + SB_V + k * 2048, TILE, 1024), i_u, k > 0 ? 1u : 0u);
-                mma_f16_ss(tmem + TU, sw128_desc(ba + SB_TL + k * 2048, TILE, 1024),
-                           sw128_desc(ba + SB_V + k * 2048, TILE, 1024), i_u, 1u);
-                mma_f16_ss(tmem + TW, sw128_desc(ba + SB_TP + k * 2048, TILE, 1024),
-                           sw128_desc(ba + SB_K + k * 2048, TILE, 1024), i_w, k > 0 ? 1u : 0u);
-            }
-#pragma unroll
-            for (int k = 0; k < GD / 16; ++k)
-                mma_f16_ss(tmem + TO1, sw128_desc(ba + SB_Q + (k >> 2) * TILE + (k & 3) * 32, 16, 1024),
-                           sw128_desc(sh_a + (k >> 2) * TILE + (k & 3) * 32, 16, 1024), i_o, k > 0 ? 1u : 0u);
-            mma_commit(bm1);
+        for (int k = 0; k < 4; ++k) {
+            mma_f16_ss(tmem + TU, th + moff(k), dv + moff(k), i_u, k > 0 ? 1u : 0u);
+            mma_f16_ss(tmem + TU, tl + moff(k), dv + moff(k), i_u, 1u);
+            mma_f16_ss(tmem + TW, tp + moff(k), dk + moff(k), i_w, k > 0 ? 1u : 0u);
         }
-        mbar_wait(bm1, (uint32_t)c & 1, abort_flag);
-        tc_fence_after();
-        // ---- -W into a K-major fp16 operand (this thread: token `row`, 64 of the 128 columns)
+    };
+    // Warps 0-3: the state (fp32, TMEM) becomes the fp16 operand image of the
+    // next chunk and is pre-scaled there by that chunk's g_C (the state update
+    // accumulates onto g_C S).  Each active thread: one state row, 128 columns.
+    auto convert_state = [&](int c_next) {
+        const float gC = reinterpret_cast<const float4 *>(buf_of(c_next) + SB_SC)[0].z;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-            float v[16];
-            tmem_ld16(tmem + tq + TW + side * 64 + q4 * 16, v);
+        for (int hh = 0; hh < 2; ++hh) {
+            float v[4][16];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) tmem_ld16(tmem + tq + TS + hh * 64 + q4 * 16, v[q4]);
             tmem_wait_ld();
             if (holds) {
 #pragma unroll
-                for (int e = 0; e < 16; e += 4)
-                    *reinterpret_cast<uint2 *>(nw + sw_off(64, row, side * 64 + q4 * 16 + e)) =
-                        pack4(-v[e], -v[e + 1], -v[e + 2], -v[e + 3]);
+                for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<uint2 *>(sh + sw_off(64, row, hh * 64 + q4 * 16 + e)) =
+                            pack4(v[q4][e], v[q4][e + 1], v[q4][e + 2], v[q4][e + 3]);
+            }
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[q4][e] *= gC;
+                tmem_st16(tmem + tq + TS + hh * 64 + q4 * 16, v[q4]);
             }
         }
+        tmem_wait_st();
+    };
+    // Warps 4-7: -W of chunk c into its K-major fp16 operand (one token row,
+    // 128 columns per active thread).
+    auto convert_w = [&]() {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            float v[4][16];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) tmem_ld16(tmem + tq + TW + hh * 64 + q4 * 16, v[q4]);
+            tmem_wait_ld();
+            if (holds) {
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<uint2 *>(nw + sw_off(64, row, hh * 64 + q4 * 16 + e)) =
+                            pack4(-v[q4][e], -v[q4][e + 1], -v[q4][e + 2], -v[q4][e + 3]);
+            }
+        }
+    };
+    // Warps 4-7: outputs of chunk c, O = (g_t/(|q_t| sqrt D)) Q S^T + Mq Delta.
+    auto readout = [&](int c) {
+        const int t = c * GC + row;
+        const float so = reinterpret_cast<const float4 *>(buf_of(c) + SB_SC)[row].x;
+        float *orow = p.out + ((size_t)t * p.Hv + h) * GD + half * 64;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            float a[2][16], bb[2][16];
+#pragma unroll
+            for (int q2 = 0; q2 < 2; ++q2) {
+                tmem_ld16(tmem + tq + TO1 + hh * 32 + q2 * 16, a[q2]);
+                tmem_ld16(tmem + tq + TO2 + hh * 32 + q2 * 16, bb[q2]);
+            }
+            tmem_wait_ld();
+            if (holds && t < p.L) {
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2)
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<float4 *>(orow + hh * 32 + q2 * 16 + e) =
+                            make_float4(a[q2][e] * so + bb[q2][e], a[q2][e + 1] * so + bb[q2][e + 1],
+                                        a[q2][e + 2] * so + bb[q2][e + 2], a[q2][e + 3] * so + bb[q2][e + 3]);
+            }
+        }
+    };
+    auto cta_sync = [&]() {
         fence_async_shared();
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
-        if (*abort_flag) break;
-        // ---- Delta = U - W S^T
+    };
+
+    // Two issuing threads: thread 0 (warp 0) issues the chain that carries
+    // the state (Delta, then the state update), thread 128 (warp 4) the
+    // products off that chain (Q S^T, and the next chunk's U and W).
+    // Prologue: chunk 0's U, W; the state image of chunk 0; -W of chunk 0.
+    // (Warps 0-3 convert state columns that warps 4-7 stored above.)
+    cta_sync();
+    mbar_wait(full, 0, abort_flag);
+    if (tid == 128) {
+        tc_fence_after();
+        issue_uw(0);
+        mma_commit(bm1);
+    }
+    if (side == 0) {
+        convert_state(0);
+    } else {
+        mbar_wait(bm1, 0, abort_flag);
+        tc_fence_after();
+        convert_w();
+    }
+    cta_sync();
+
+    for (int c = 0; c < p.nch && !*abort_flag; ++c) {
+        const uint32_t ba = smem_addr(buf_of(c));
+        // ---- Delta = U - W S^T (thread 0) and O1 = Q S^T (thread 128)
         if (tid == 0) {
-            const uint32_t i_d = idesc_f16(64, 64, false, false);
+#pragma unroll
+            for (int k = 0; k < GD / 16; ++k) mma_f16_ss(tmem + TU, d_nw + koff(k), d_sh + koff(k), i_d, 1u);
+            mma_commit(bm3);
+        } else if (tid == 128) {
+            const uint64_t dq = kmaj(ba + SB_Q);
 #pragma unroll
             for (int k = 0; k < GD / 16; ++k)
-                mma_f16_ss(tmem + TU, sw128_desc(nw_a + (k >> 2) * TILE + (k & 3) * 32, 16, 1024),
-                           sw128_desc(sh_a + (k >> 2) * TILE + (k & 3) * 32, 16, 1024), i_d, 1u);
-            mma_commit(bm3);
+                mma_f16_ss(tmem + TO1, dq + koff(k), d_sh + koff(k), i_d, k > 0 ? 1u : 0u);
+            mma_commit(bm4);
         }
         mbar_wait(bm3, (uint32_t)c & 1, abort_flag);
         tc_fence_after();
-        // ---- Delta (fp16, for Mq Delta) and Delta' = Delta * (g_C/g_t)/|k_t| (hi + lo, for the
-        //      state update), both [tokens][Dv] images; state scaled by g_C in TMEM.
+        // ---- Delta (fp16, for Mq Delta) and Delta' = Delta (g_C/g_t)/|k_t| (hi + lo, for the
+        //      state update), both [tokens][Dv] images; this thread: 32 of the 64 columns.
         {
-            const float4 sc = reinterpret_cast<const float4 *>(buf + SB_SC)[row];
-            const float gC = reinterpret_cast<const float4 *>(buf + SB_SC)[0].z;
+            const float sy = reinterpret_cast<const float4 *>(buf_of(c) + SB_SC)[row].y;
+            float dv[2][16];
 #pragma unroll
-            for (int q2 = 0; q2 < 2; ++q2) {
-                float v[16];
-                tmem_ld16(tmem + tq + TU + side * 32 + q2 * 16, v);
-                tmem_wait_ld();
-                if (holds) {
+            for (int q2 = 0; q2 < 2; ++q2) tmem_ld16(tmem + tq + TU + side * 32 + q2 * 16, dv[q2]);
+            tmem_wait_ld();
+            if (holds) {
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2)
 #pragma unroll
                     for (int e = 0; e < 16; e += 4) {
-                        const int col = side * 32 + q2 * 16 + e;          // Dv column within the half
-                        const uint32_t off = sw_off(64, row, col);        // [tokens rows][64 Dv], one block
-                        *reinterpret_cast<uint2 *>(dl + off) = pack4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-                        float d[4] = {v[e] * sc.y, v[e + 1] * sc.y, v[e + 2] * sc.y, v[e + 3] * sc.y};
+                        const float *v = dv[q2] + e;
+                        const uint32_t off = sw_off(64, row, side * 32 + q2 * 16 + e);
+                        *reinterpret_cast<uint2 *>(dl + off) = pack4(v[0], v[1], v[2], v[3]);
                         float hh[4], ll[4];
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) { hh[u] = __half2float(__float2half_rn(d[u])); ll[u] = d[u] - hh[u]; }
+                        for (int u = 0; u < 4; ++u) {
+                            const float d = v[u] * sy;
+                            hh[u] = __half2float(__float2half_rn(d));
+                            ll[u] = d - hh[u];
+                        }
                         *reinterpret_cast<uint2 *>(dhi + off) = pack4(hh[0], hh[1], hh[2], hh[3]);
                         *reinterpret_cast<uint2 *>(dlo + off) = pack4(ll[0], ll[1], ll[2], ll[3]);
                     }
-                }
             }
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-                float v[16];
-                tmem_ld16(tmem + tq + TS + side * 64 + q4 * 16, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] *= gC;
-                tmem_st16(tmem + tq + TS + side * 64 + q4 * 16, v);
-            }
-            tmem_wait_st();
         }
-        fence_async_shared();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (*abort_flag) break;
-        // ---- O2 = Mq Delta;  S += Delta'^T K
+        cta_sync();
+        // ---- O2 = Mq Delta and S = g_C S + Delta'^T K (thread 0); U, W of the next chunk (thread 128)
         if (tid == 0) {
-            const uint32_t i_m = idesc_f16(64, 64, false, true), i_s = idesc_f16(64, 128, true, true);
+            const uint64_t dmq = kmaj(ba + SB_MQ), dk = mnmaj(ba + SB_K);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                mma_f16_ss(tmem + TO2, sw128_desc(ba + SB_MQ + k * 32, 16, 1024),
-                           sw128_desc(dl_a + k * 2048, TILE, 1024), i_m, k > 0 ? 1u : 0u);
-                mma_f16_ss(tmem + TS, sw128_desc(dh_a + k * 2048, TILE, 1024),
-                           sw128_desc(ba + SB_K + k * 2048, TILE, 1024), i_s, 1u);
-                mma_f16_ss(tmem + TS, sw128_desc(dlo_a + k * 2048, TILE, 1024),
-                           sw128_desc(ba + SB_K + k * 2048, TILE, 1024), i_s, 1u);
+                mma_f16_ss(tmem + TO2, dmq + (uint64_t)(k * 2), d_dl + moff(k), i_m, k > 0 ? 1u : 0u);
+                mma_f16_ss(tmem + TS, d_dh + moff(k), dk + moff(k), i_s, 1u);
+                mma_f16_ss(tmem + TS, d_dlo + moff(k), dk + moff(k), i_s, 1u);
             }
             mma_commit(bm5);
+        } else if (tid == 128 && c + 1 < p.nch) {
+            if (mbar_wait(full + ((c + 1) & 1), (uint32_t)((c + 1) >> 1) & 1, abort_flag)) {
+                tc_fence_after();
+                issue_uw(c + 1);
+            }
+            mma_commit(bm1);
         }
+        // ---- warps 0-3: next state image (+ g_C scaling); warps 4-7: outputs, next -W
         mbar_wait(bm5, (uint32_t)c & 1, abort_flag);
+        mbar_wait(bm4, (uint32_t)c & 1, abort_flag);      // Q S^T has read the state image
         tc_fence_after();
-        // ---- outputs O = (g_t/(|q_t| sqrt D)) Q S^T + Mq Delta, then the new state's fp16 image
-        {
-            const int t = c * GC + row;
-            const float so = reinterpret_cast<const float4 *>(buf + SB_SC)[row].x;
-            float *orow = p.out + ((size_t)t * p.Hv + h) * GD + half * 64 + side * 32;
-#pragma unroll
-            for (int q2 = 0; q2 < 2; ++q2) {
-                float a[16], bb[16];
-                tmem_ld16(tmem + tq + TO1 + side * 32 + q2 * 16, a);
-                tmem_ld16(tmem + tq + TO2 + side * 32 + q2 * 16, bb);
-                tmem_wait_ld();
-                if (holds && t < p.L) {
-#pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4 *>(orow + q2 * 16 + e) =
-                            make_float4(a[e] * so + bb[e], a[e + 1] * so + bb[e + 1], a[e + 2] * so + bb[e + 2],
-                                        a[e + 3] * so + bb[e + 3]);
-                }
+        if (side == 0) {
+            if (c + 1 < p.nch) {
+                mbar_wait(full + ((c + 1) & 1), (uint32_t)((c + 1) >> 1) & 1, abort_flag);
+                convert_state(c + 1);
             }
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-                float v[16];
-                tmem_ld16(tmem + tq + TS + side * 64 + q4 * 16, v);
-                tmem_wait_ld();
-                if (holds) {
-#pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<uint2 *>(sh + sw_off(64, row, side * 64 + q4 * 16 + e)) =
-                            pack4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-                }
+        } else {
+            readout(c);
+            if (c + 1 < p.nch) {
+                mbar_wait(bm1, (uint32_t)(c + 1) & 1, abort_flag);
+                tc_fence_after();
+                convert_w();
             }
         }
-        fence_async_shared();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (*abort_flag) break;
+        cta_sync();
+        // This chunk's buffer is free again: the loads of chunk c+2 go into it.
+        if (tid == 0 && c + 2 < p.nch) { issue_loads(c + 2); last_issued = c + 2; }
     }
     // Final state rows back to global memory (fp32).
     if (!*abort_flag) {
@@ -527,7 +627,7 @@ gdn_scan_kernel(const __grid_constant__ CUtensorMap mTh, const __grid_constant__
     // Every issued load must land before the CTA may exit.
     if (tid == 0) {
         const long long t0 = clock64();
-        for (int c = max(0, p.nch - 2); c < p.nch; ++c)
+        for (int c = max(0, last_issued - 1); c <= last_issued; ++c)
             while (!mbar_try_wait(full + (c & 1), (uint32_t)(c >> 1) & 1) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
     }
     tc_fence_before();
