@@ -142,11 +142,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volati
 }
 
 template <bool PRECISE>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(PRECISE ? 256 : 384, 1)
 fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
           const FaParams p) {
     using L = FaLayout<PRECISE>;
     constexpr int QROWS = L::QROWS;
+    constexpr int SOFT_WARPS = PRECISE ? 4 : 8;                // softmax warps
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023) {           // 128B-swizzle atoms need a 1024-byte aligned base
         if (threadIdx.x == 0) raise_status(STATUS_BAD_ARGUMENT);
@@ -155,9 +156,10 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::SM_BAR);
     uint64_t *k_full = bars, *v_full = bars + 3, *k_empty = bars + 6, *v_empty = bars + 9,
              *s_full = bars + 12, *s_free = bars + 14, *p_full = bars + 16, *p_free = bars + 18,
-             *mma_done = bars + 20, *q_ready = bars + 21, *app_done = bars + 22;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::SM_BAR + 192);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::SM_BAR + 196);
+             *mma_done = bars + 20, *q_ready = bars + 21, *app_done = bars + 22, *xbar = bars + 23,
+             *lbar = bars + 25;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::SM_BAR + 224);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::SM_BAR + 228);
     float2 *rope = reinterpret_cast<float2 *>(smem + L::SM_ROPE);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -191,11 +193,13 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             mbar_init(k_empty + i, 1); mbar_init(v_empty + i, 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(s_full + i, 1); mbar_init(s_free + i, 4);
-            mbar_init(p_full + i, 4); mbar_init(p_free + i, 1);
+            mbar_init(s_full + i, 1); mbar_init(s_free + i, SOFT_WARPS);
+            mbar_init(p_full + i, SOFT_WARPS); mbar_init(p_free + i, 1);
+            mbar_init(xbar + i, SOFT_WARPS);
         }
         mbar_init(mma_done, 1);
-        mbar_init(q_ready, p.fused ? 8 : 4);      // every warp (fused) or the softmax warps
+        mbar_init(q_ready, p.fused ? 8 : 4);      // every warp (fused) or softmax warps 4-7
+        mbar_init(lbar, 4);
         mbar_init(app_done, 64);
         *abort_flag = 0;
         fence_barrier_init();
@@ -207,10 +211,12 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // Softmax warps 4-7: thread = TMEM lane = A row of the QK MMA.
-    // FAST: A row = query row.  PRECISE: lanes i and i+16 of warp w carry the
-    // hi and lo halves of query row 16w+i (one M=128 MMA yields both).
-    const int wq = warp - 4;
+    // Softmax warps 4-7 (and 8-11 in FAST): thread = TMEM lane = A row of the
+    // QK MMA.  FAST: A row = query row; warpgroup wg (warps 4-7 / 8-11) takes
+    // columns [32 wg, 32 wg + 32) of every S tile.  PRECISE: lanes i and i+16
+    // of warp w carry the hi and lo halves of query row 16w+i (one M=128 MMA
+    // yields both).
+    const int wq = (warp - 4) & 3, wg = PRECISE ? 0 : ((warp - 4) >> 2);
     const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
     const int half = PRECISE ? (lane >> 4) : 0;
     const int r = PRECISE ? wq * 16 + (lane & 15) : wq * 32 + lane;     // logical query row
@@ -354,7 +360,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             fence_async_global();
             mbar_arrive(app_done);
         }
-    } else if (warp >= 4) {
+    } else if (warp >= 4 && warp < 8) {
         // Stage this lane's prepared query row (256 fp16 = 128 columns) into TMEM.
         const __half *src = (PRECISE && half) ? p.q_lo : p.q;
         const uint4 *row = reinterpret_cast<const uint4 *>(src + ((size_t)t * NQ + h) * HD);
@@ -417,10 +423,16 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 const uint32_t pa = smem_addr(smem + L::SM_P + b * 128 * 128);
                 const uint32_t vb = smem_addr(smem + L::SM_KV + s * L::SM_KV_STAGE + TILE_BYTES);
 #pragma unroll
-                for (int k = 0; k < BN / 16; ++k)
-                    mma_f16_ss(tmem + TM_O, sw128_desc(pa + k * 32, 16, 1024),
-                               sw128_desc(vb + k * 16 * 128, BN * 128, 1024), idesc_pv,
-                               (i > 0 || k > 0) ? 1u : 0u);
+                for (int k = 0; k < BN / 16; ++k) {
+                    if (PRECISE)      // P (hi / lo rows) from shared memory
+                        mma_f16_ss(tmem + TM_O, sw128_desc(pa + k * 32, 16, 1024),
+                                   sw128_desc(vb + k * 16 * 128, BN * 128, 1024), idesc_pv,
+                                   (i > 0 || k > 0) ? 1u : 0u);
+                    else              // P written over its S tile in TMEM (fp16, 2 per column)
+                        mma_f16_ts(tmem + TM_O, tmem + TM_S + b * BN + k * 8,
+                                   sw128_desc(vb + k * 16 * 128, BN * 128, 1024), idesc_pv,
+                                   (i > 0 || k > 0) ? 1u : 0u);
+                }
                 mma_commit(p_free + b);
                 mma_commit(v_empty + s);
                 return true;
@@ -430,7 +442,12 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             for (int j = 0; j < ntiles && ok; ++j) {
                 const int b = j & 1, s = j % STAGES3;
                 if (!mbar_wait(k_full + s, (j / STAGES3) & 1, abort_flag)) { ok = false; break; }
-                if (j >= 2 && !mbar_wait(s_free + b, ((j >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
+                // S buffer b is reusable once the softmax has read tile j-2.  FAST:
+                // implied by the p_full wait before PV(j-2) (issued above by this
+                // thread), and tile j-2's P, kept in this buffer, is read by PV(j-2)
+                // before this QK writes it: tcgen05.mma issued by one thread execute
+                // in issue order.
+                if (PRECISE && j >= 2 && !mbar_wait(s_free + b, ((j >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t kb = smem_addr(smem + L::SM_KV + s * L::SM_KV_STAGE);
 #pragma unroll
@@ -450,11 +467,16 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         }
     } else if (warp >= 4) {
         // ------------------------------------------------ softmax + epilogue
-        // FAST: each thread owns a query row and all 64 columns of a tile.
+        // Each thread handles 32 columns of its row per tile.  FAST: warpgroup
+        // wg takes columns [32 wg, 32 wg + 32); the two warpgroups agree on the
+        // row maximum through a shared-memory exchange (an mbarrier per S
+        // buffer) and keep separate row sums, added after the last tile.
         // PRECISE: lane i keeps columns [0,32) and lane i+16 columns [32,64) of
         // row 16w+i, each summing the hi and lo score halves, and each writes
         // the hi and lo probabilities of its columns.
-        constexpr int NC = PRECISE ? 32 : 64;                      // columns per thread
+        constexpr int NC = 32;                                     // columns per thread
+        const int cpart = PRECISE ? half : wg;                     // which 32 columns
+        float *xch = reinterpret_cast<float *>(smem + L::SM_ROPE);  // FAST: [2 buffers][2 wg][128 rows]
         const int pos_limit = valid ? p.position + t - p.kv_begin : -1;   // last visible local row
         const int arow_hi = PRECISE ? wq * 32 + (lane & 15) : r;         // A rows of P (hi, lo)
         const int arow_lo = arow_hi + 16;
@@ -465,8 +487,15 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             if (!warp_wait(s_full + b, (j >> 1) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
             float x[64];
+            if (PRECISE) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld16(t_lane + TM_S + b * BN + c * 16, *reinterpret_cast<float(*)[16]>(x + c * 16));
+                for (int c = 0; c < 4; ++c)
+                    tmem_ld16(t_lane + TM_S + b * BN + c * 16, *reinterpret_cast<float(*)[16]>(x + c * 16));
+            } else {
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+                    tmem_ld16(t_lane + TM_S + b * BN + wg * 32 + c * 16, *reinterpret_cast<float(*)[16]>(x + c * 16));
+            }
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
@@ -478,25 +507,41 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                     x[c] = (half ? x[32 + c] : x[c]) + recv;
                 }
             }
-            const int key0 = (tile0 + j) * BN + half * 32;
+            const int key0 = (tile0 + j) * BN + cpart * 32;
             const int lim = min(pos_limit, p.kv_rows - 1) - key0;     // columns <= lim are visible
-            float m_tile = -INFINITY;
+            // Row max and (below) row sum over 8 / 4 independent partials, so
+            // neither is one long dependent chain.
+            float mp[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) mp[q] = -INFINITY;
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
                 x[c] = c <= lim ? x[c] : -INFINITY;
-                m_tile = fmaxf(m_tile, x[c]);
+                mp[c & 7] = fmaxf(mp[c & 7], x[c]);
             }
-            if (PRECISE) m_tile = fmaxf(m_tile, __shfl_xor_sync(0xffffffffu, m_tile, 16));
+            float m_tile = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                                 fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+            if (PRECISE) {
+                m_tile = fmaxf(m_tile, __shfl_xor_sync(0xffffffffu, m_tile, 16));
+            } else {
+                xch[(b * 2 + wg) * 128 + r] = m_tile;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(xbar + b);
+                if (!warp_wait(xbar + b, (j >> 1) & 1, abort_flag)) { ok = false; break; }
+                m_tile = fmaxf(m_tile, xch[(b * 2 + (wg ^ 1)) * 128 + r]);
+            }
             m_tile *= SCORE_LOG2;                                  // log2 units (-inf stays -inf)
             float factor = 1.f;
             const bool need = m_tile > m_use + RESCALE_THRESHOLD;
             if (need) { factor = exp2_approx(m_use - m_tile); m_use = m_tile; l *= factor; }
             if (j > 0 && __any_sync(0xffffffffu, need)) {
-                // O already holds tiles < j: wait for PV(j-1), then rescale rows in TMEM.
+                // O already holds tiles < j: wait for PV(j-1), then rescale rows in
+                // TMEM (FAST: each warpgroup its half of the columns).
                 if (!warp_wait(p_free + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
+                constexpr int CH = PRECISE ? HD / 16 : HD / 32;
 #pragma unroll 1
-                for (int c = 0; c < HD / 16; ++c) {
+                for (int c = wg * CH; c < wg * CH + CH; ++c) {
                     float o[16];
                     tmem_ld16(t_lane + TM_O + c * 16, o);
                     tmem_wait_ld();
@@ -508,7 +553,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             }
             const float mref = m_use == -INFINITY ? 0.f : m_use;
             uint32_t hi[NC / 2], lo[PRECISE ? NC / 2 : 1];
-            float sum = 0.f;
+            float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < NC; c += 2) {
                 const float p0 = exp2_approx(fmaf(x[c], SCORE_LOG2, -mref));
@@ -520,32 +565,48 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                     const __half2 lp = __floats2half2_rn(p0 - back.x, p1 - back.y);
                     lo[c / 2] = *reinterpret_cast<const uint32_t *>(&lp);
                 }
-                sum += p0 + p1;
+                sp[(c >> 1) & 3] += p0 + p1;
             }
-            l += sum;
-            if (j >= 2 && !warp_wait(p_free + b, ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
-            uint8_t *pbuf = smem + L::SM_P + b * 128 * 128;
+            l += (sp[0] + sp[1]) + (sp[2] + sp[3]);
             if (PRECISE) {
+                if (j >= 2 && !warp_wait(p_free + b, ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
+                uint8_t *pbuf = smem + L::SM_P + b * 128 * 128;
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
-                    const int unit = half * 4 + w;
+                    const int unit = cpart * 4 + w;
                     *reinterpret_cast<uint4 *>(pbuf + arow_hi * 128 + ((unit ^ (arow_hi & 7)) << 4)) =
                         make_uint4(hi[4 * w], hi[4 * w + 1], hi[4 * w + 2], hi[4 * w + 3]);
                     *reinterpret_cast<uint4 *>(pbuf + arow_lo * 128 + ((unit ^ (arow_lo & 7)) << 4)) =
                         make_uint4(lo[4 * w], lo[4 * w + 1], lo[4 * w + 2], lo[4 * w + 3]);
                 }
+                fence_async_shared();
             } else {
-#pragma unroll
-                for (int w = 0; w < 8; ++w)
-                    *reinterpret_cast<uint4 *>(pbuf + arow_hi * 128 + ((w ^ (arow_hi & 7)) << 4)) =
-                        make_uint4(hi[4 * w], hi[4 * w + 1], hi[4 * w + 2], hi[4 * w + 3]);
+                // fp16 P of columns [32 wg, 32 wg + 32) into TMEM columns [16 wg, 16 wg + 16)
+                // of this S buffer: S columns both warpgroups have read (they passed
+                // the exchange), and which the QK MMA rewrites only after this
+                // tile's PV (issued earlier by the same thread) has consumed them.
+                tmem_st16(t_lane + TM_S + b * BN + wg * 16, *reinterpret_cast<const float(*)[16]>(hi));
+                tmem_wait_st();
             }
-            fence_async_shared();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + b);
         }
         if (PRECISE) l += __shfl_xor_sync(0xffffffffu, l, 16);
+        if (!PRECISE) {
+            // Warpgroup 1 hands its row sums to warpgroup 0, which writes the output.
+            float *lx = xch + (ntiles & 1) * 256;     // the exchange buffer no tile still reads
+            if (wg == 1) {
+                lx[r] = l;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(lbar);
+                ok = false;                            // the epilogue is warpgroup 0's
+            } else if (ok && warp_wait(lbar, 0, abort_flag)) {
+                l += lx[r];
+            } else {
+                ok = false;
+            }
+        }
         // Epilogue: the final PV's commit on p_free marks O complete (and every
         // K/V tile consumed, so the ring is idle).  O leaves through shared
         // memory: every lane puts its TMEM lane (PRECISE: O_hi in lanes i,
@@ -926,7 +987,7 @@ bool decode_regime(int T) { return T * GROUP <= DECODE_ROWS; }
 
 template <bool PRECISE>
 void launch_fa(const CUtensorMap &mk, const CUtensorMap &mv, const FaParams &p, dim3 grid, cudaStream_t st) {
-    const cudaError_t e = launch_chained(fa_kernel<PRECISE>, grid, dim3(256), FaLayout<PRECISE>::SMEM_BYTES, st,
+    const cudaError_t e = launch_chained(fa_kernel<PRECISE>, grid, dim3(PRECISE ? 256 : 384), FaLayout<PRECISE>::SMEM_BYTES, st,
                                          mk, mv, p);
     if (e != cudaSuccess) throw std::runtime_error(std::string("attention kernel launch: ") + cudaGetErrorString(e));
 }
