@@ -227,13 +227,19 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     grid_dependency_wait();
     if (threadIdx.x == 0) launch_dependents();
 
-    // Fused decode: K of tile 0 goes out before the queries are prepared
-    // (unless that tile holds new rows, which must be written first).
-    const bool k0_early = PRECISE && p.fused && app_tile > 0 && ntiles > 0;
-    if (k0_early && threadIdx.x == 0) {
-        mbar_expect_tx(k_full, TILE_BYTES);
-        for (int c = 0; c < 4; ++c)
-            tma_load_2d(smem + L::SM_KV + c * BN * 128, &tmK, k_full, kv_head * HD + c * 64, tile0 * BN);
+    // Fused decode: tiles 0 and 1 (stages 0 and 1) go out before the queries
+    // are prepared, unless they hold new rows, which must be written first;
+    // stage 2 stages the queries, so tile 2 waits for them.
+    const int early = (PRECISE && p.fused) ? min(ntiles, min(app_tile, 2)) : 0;
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < early; ++j) {
+            uint8_t *kd = smem + L::SM_KV + j * L::SM_KV_STAGE, *vd = kd + TILE_BYTES;
+            const int y = (tile0 + j) * BN;
+            mbar_expect_tx(k_full + j, TILE_BYTES);
+            for (int c = 0; c < 4; ++c) tma_load_2d(kd + c * BN * 128, &tmK, k_full + j, kv_head * HD + c * 64, y);
+            mbar_expect_tx(v_full + j, TILE_BYTES);
+            for (int c = 0; c < 4; ++c) tma_load_2d(vd + c * BN * 128, &tmV, v_full + j, kv_head * HD + c * 64, y);
+        }
     }
 
     if (PRECISE && p.fused) {
@@ -243,8 +249,8 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         // 11 significant bits, so that lo = x - hi is exact), written in TMEM
         // A-row order (hi of row 16g+i at A row 32g+i, lo at 32g+16+i; 512 bytes
         // per A row, 16-byte chunks XOR-swizzled by the row's low 3 bits) into
-        // the second K/V stage, which the producer leaves idle until the
-        // queries are staged.  Each warp then copies half the columns of its
+        // the third K/V stage, which the producer leaves idle until the
+        // queries are staged (tiles 0 and 1 are already on their way).  Each warp then copies half the columns of its
         // TMEM lane quarter; warps 2-3 finally write the block's new keys /
         // values, if this CTA's tiles hold them.  Lane l of a row holds dims
         // [4l,4l+4) and [128+4l,128+4l+4).
@@ -276,7 +282,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
 #pragma unroll
             for (int j = 0; j < QR; ++j) ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], o);
         }
-        uint8_t *qstage = smem + L::SM_KV + L::SM_KV_STAGE;
+        uint8_t *qstage = smem + L::SM_KV + 2 * L::SM_KV_STAGE;     // third K/V stage
         const int sub = (lane & 1) * 8;
         auto split = [](float a, float b, uint32_t &hi, uint32_t &lo) {
             const float ha = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
@@ -382,22 +388,19 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         // K tiles are released after QK, V tiles after PV, so the next K load
         // overlaps the softmax and PV of the current tile.
         if (lane == 0) {
-            int k_issued = 0, v_issued = 0;
-            for (int j = 0; j < ntiles; ++j) {
+            int k_issued = early, v_issued = early;        // tiles issued before the query preparation
+            for (int j = early; j < ntiles; ++j) {
                 const int s = j % STAGES3;
                 const uint32_t use = (uint32_t)(j / STAGES3);
                 const int y = (tile0 + j) * BN;
                 uint8_t *kd = smem + L::SM_KV + s * L::SM_KV_STAGE, *vd = kd + TILE_BYTES;
                 if (j == app_tile && !mbar_wait(app_done, 0, abort_flag)) break;   // new rows written
                 if (j >= STAGES3 && !mbar_wait(k_empty + s, (use - 1) & 1, abort_flag)) break;
-                if (j > 0 || !k0_early) {
-                    mbar_expect_tx(k_full + s, TILE_BYTES);
-                    for (int c = 0; c < 4; ++c) tma_load_2d(kd + c * BN * 128, &tmK, k_full + s, kv_head * HD + c * 64, y);
-                }
+                // Fused decode: stage 2 holds the staged queries until they are in TMEM.
+                if (PRECISE && p.fused && j == 2 && !mbar_wait(q_ready, 0, abort_flag)) break;
+                mbar_expect_tx(k_full + s, TILE_BYTES);
+                for (int c = 0; c < 4; ++c) tma_load_2d(kd + c * BN * 128, &tmK, k_full + s, kv_head * HD + c * 64, y);
                 k_issued = j + 1;
-                // The queries' loads go out ahead of the K/V stream: only K of
-                // tile 0 is requested until they are staged.
-                if (j == 0 && !mbar_wait(q_ready, 0, abort_flag)) break;
                 if (j >= STAGES3 && !mbar_wait(v_empty + s, (use - 1) & 1, abort_flag)) break;
                 mbar_expect_tx(v_full + s, TILE_BYTES);
                 for (int c = 0; c < 4; ++c) tma_load_2d(vd + c * BN * 128, &tmV, v_full + s, kv_head * HD + c * 64, y);
