@@ -101,6 +101,20 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
     grid_dependency_wait();
     if (tid == 0) launch_dependents();
 
+    // Raw decay inputs of this lane's two tokens (warp 0), loaded with the
+    // keys / queries so that both arrive in one round trip.
+    float al_raw[2] = {0.f, 0.f}, be_raw[2] = {0.f, 0.f};
+    if (warp == 0) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int t = 2 * lane + e;
+            if (t < n) {
+                const size_t idx = (size_t)(t0 + t) * p.Hv + h;
+                al_raw[e] = p.alpha[idx];
+                be_raw[e] = p.beta[idx];
+            }
+        }
+    }
     // (1) normalised keys / queries as fp16 MMA operands: warp w takes tokens
     //     16w..16w+15, lane l dims [4l, 4l+4); the 32 sums reduce together.
     {
@@ -158,9 +172,8 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
             const int t = 2 * lane + e;
             g[e] = 0.f; b[e] = 0.f;
             if (t < n) {
-                const size_t idx = (size_t)(t0 + t) * p.Hv + h;
-                g[e] = dh * softplusf_(p.alpha[idx] + bh) * 1.4426950408889634f;
-                b[e] = sigmoidf_(p.beta[idx]);
+                g[e] = dh * softplusf_(al_raw[e] + bh) * 1.4426950408889634f;
+                b[e] = sigmoidf_(be_raw[e]);
             }
         }
         float s = g[0] + g[1];
