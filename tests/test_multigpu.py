@@ -1,6 +1,6 @@
-"""Sequence-split verify across two GPUs through the library's fused peer-memory
+"""Sequence-split verify across two or four GPUs through the library's fused peer-memory
 exchange (and the NCCL all-gather variant), compared with the single-device
-CPU oracle.  Needs two GPUs; skipped on single-GPU machines."""
+CPU oracle.  Each case is skipped on machines with fewer GPUs than its ranks."""
 import datetime
 import os
 import queue
@@ -67,21 +67,23 @@ def _worker(rank, world, port, position, batch, mode, result):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(_gpus() < 2, reason='needs two GPUs')
+@pytest.mark.parametrize('world', [2, 4])
 @pytest.mark.parametrize('mode', ['peer', 'nccl'])
-def test_two_gpu_sequence_split_verify(mode):
+def test_sequence_split_verify(mode, world):
+    if _gpus() < world:
+        pytest.skip(f'needs {world} GPUs')
     import torch.multiprocessing as mp
     position, batch = 70000, 8
     ctx = mp.get_context('spawn')
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, position, batch, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, position, batch, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = []
     try:
         deadline = time.time() + 300
-        while len(got) < 2 and time.time() < deadline:
+        while len(got) < world and time.time() < deadline:
             try:
                 got.append(q.get(timeout=5))
             except queue.Empty:
@@ -93,7 +95,7 @@ def test_two_gpu_sequence_split_verify(mode):
             if p.exitcode is None:
                 p.kill()
     assert all(p.exitcode == 0 for p in procs)
-    assert len(got) == 2
+    assert len(got) == world
     c = I.attention_layer(batch=batch, position=position, seed=91)
     exp, _, _ = oracle.attention(**c)
     for rank, status, out in got:
