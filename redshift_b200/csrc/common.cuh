@@ -140,18 +140,6 @@ __device__ __forceinline__ void grid_dependency_wait() {
 __device__ __forceinline__ void launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
-// L2 prefetch of the 128-byte lines of [p, p + bytes), spread over `nthreads`
-// threads.  A prefetch only moves lines into L2, the point of coherence, so it
-// may be issued before grid_dependency_wait(): loads after the wait still see
-// the previous kernel's writes, while the DRAM latency of inputs the kernel
-// will read overlaps the previous kernel's tail.
-__device__ __forceinline__ void prefetch_l2(const void *p) {
-    asm volatile("prefetch.global.L2 [%0];" :: "l"(p));
-}
-__device__ __forceinline__ void prefetch_l2_range(const void *p, size_t bytes, int tid, int nthreads) {
-    const char *c = static_cast<const char *>(p);
-    for (size_t off = (size_t)tid * 128; off < bytes; off += (size_t)nthreads * 128) prefetch_l2(c + off);
-}
 
 // Named barrier over a subset of the CTA's warps (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
