@@ -224,24 +224,61 @@ class Step:
     # host-side (pinned) copies of the per-step inputs and outputs, for e2e
     def host_mirror(self):
         torch = self.torch
-        self.h_in, self.h_out = [], []
+        self.h_in_attn, self.h_in_delta, self.h_out_attn, self.h_out_delta = [], [], [], []
         for a in self.attn:
-            self.h_in.append([(a[k], a[k].cpu().pin_memory()) for k in ('q_gate', 'key', 'value')])
-            self.h_out.append((a['out'], torch.empty_like(a['out'], device='cpu').pin_memory()))
+            self.h_in_attn.append([(a[k], a[k].cpu().pin_memory()) for k in ('q_gate', 'key', 'value')])
+            self.h_out_attn.append((a['out'], torch.empty_like(a['out'], device='cpu').pin_memory()))
         for d in self.delta:
-            self.h_in.append([(d[k], d[k].cpu().pin_memory()) for k in ('qkv', 'gate', 'alpha', 'beta')])
-            self.h_out.append((d['out'], torch.empty_like(d['out'], device='cpu').pin_memory()))
-        h2d = sum(h.numel() * h.element_size() for group in self.h_in for _, h in group)
-        d2h = sum(h.numel() * h.element_size() for _, h in self.h_out)
+            self.h_in_delta.append([(d[k], d[k].cpu().pin_memory()) for k in ('qkv', 'gate', 'alpha', 'beta')])
+            self.h_out_delta.append((d['out'], torch.empty_like(d['out'], device='cpu').pin_memory()))
+        self.s_in, self.s_out = torch.cuda.Stream(), torch.cuda.Stream()
+        groups = self.h_in_attn + self.h_in_delta
+        h2d = sum(h.numel() * h.element_size() for group in groups for _, h in group)
+        d2h = sum(h.numel() * h.element_size() for _, h in self.h_out_attn + self.h_out_delta)
         return h2d, d2h
 
     def run_e2e(self):
-        for group in self.h_in:
-            for dev, host in group:
-                dev.copy_(host, non_blocking=True)
-        self.run()
-        for dev, host in self.h_out:
-            host.copy_(dev, non_blocking=True)
+        """One step through the public API from pinned host buffers: every layer's
+        inputs are copied host->device on a copy stream in layer order (each layer
+        waits only for its own inputs), and every layer's output is read back on a
+        second copy stream as soon as the layer is done; the step ends when the
+        last read-back has landed."""
+        torch = self.torch
+        main = torch.cuda.current_stream()
+        start = torch.cuda.Event()
+        start.record(main)
+        self.s_in.wait_event(start)
+        self.s_out.wait_event(start)
+        ready, ai, di = [], 0, 0
+        with torch.cuda.stream(self.s_in):
+            for layer in range(LAYERS):
+                if layer % 4 == 3:
+                    group, ai = self.h_in_attn[ai], ai + 1
+                else:
+                    group, di = self.h_in_delta[di], di + 1
+                for dev, host in group:
+                    dev.copy_(host, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self.s_in)
+                ready.append(ev)
+        ai = di = 0
+        for layer in range(LAYERS):
+            main.wait_event(ready[layer])
+            if layer % 4 == 3:
+                self.attention_layer(self.attn[ai], slot=ai & 1)
+                dev, host = self.h_out_attn[ai]
+                ai += 1
+            else:
+                self.delta_layer(self.delta[di])
+                dev, host = self.h_out_delta[di]
+                di += 1
+            done = torch.cuda.Event()
+            done.record(main)
+            self.s_out.wait_event(done)
+            with torch.cuda.stream(self.s_out):
+                host.copy_(dev, non_blocking=True)
+        main.wait_stream(self.s_in)
+        main.wait_stream(self.s_out)
 
 
 def make_events(n, external):
