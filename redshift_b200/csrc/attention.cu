@@ -860,22 +860,32 @@ attn_exchange_kernel(float *out, const float *part_o, const float *part_ml, int 
         if (d == 0) st_word_sys(dst + HD, tag | __float_as_uint(lse));
     }
 
-    // ---- receive the other ranks' partials of the row and merge
+    // ---- receive the other ranks' partials of the row and merge.  The words of
+    //      all peers are read at once, so their latencies overlap; a word whose
+    //      flag is not there yet is re-read until it is (bounded).
     uint64_t *own = reinterpret_cast<uint64_t *>(peers[rank]);
     const long long t0 = clock64();
     bool ok = true;
-    auto take = [&](uint64_t *word, float &value) {
-        uint64_t x = ld_word_sys(word);
+    auto finish = [&](uint64_t *word, uint64_t x, float fallback) {
         while ((uint32_t)(x >> 32) != EX_FLAG) {
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok = false; return; }
+            if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok = false; return fallback; }
             x = ld_word_sys(word);
         }
-        value = __uint_as_float((uint32_t)x);
         *word = 0;
+        return __uint_as_float((uint32_t)x);
     };
+    auto word_of = [&](int q, int col) {
+        return own + (((size_t)slot * world + q) * EX_ROWS + row) * EX_WORDS + col;
+    };
+    uint64_t first[EX_MAX_WORLD], lse_first = 0;
+    const bool lse_reader = d < world && d != rank;
+    if (lse_reader) lse_first = ld_word_sys(word_of(d, HD));
+#pragma unroll
+    for (int q = 0; q < EX_MAX_WORLD; ++q)
+        first[q] = (q < world && q != rank) ? ld_word_sys(word_of(q, d)) : 0;
     if (d < world) {
         float x = lse;
-        if (d != rank) take(own + (((size_t)slot * world + d) * EX_ROWS + row) * EX_WORDS + HD, x);
+        if (lse_reader) x = finish(word_of(d, HD), lse_first, x);
         lse_s[d] = x;
     }
     float val[EX_MAX_WORLD];
@@ -884,7 +894,7 @@ attn_exchange_kernel(float *out, const float *part_o, const float *part_ml, int 
         val[q] = 0.f;
         if (q < world) {
             if (q == rank) val[q] = o;
-            else take(own + (((size_t)slot * world + q) * EX_ROWS + row) * EX_WORDS + d, val[q]);
+            else val[q] = finish(word_of(q, d), first[q], 0.f);
         }
     }
     const int all_ok = __syncthreads_and(ok);
