@@ -80,7 +80,7 @@ constexpr int BMS = 68;                          // row stride: 16-byte rows, co
 constexpr int PREP_SMALL = PREP_BM + 64 * BMS * 4;
 constexpr int PREP_SMEM = PREP_SMALL + 4 * 64 * 4 + 64;
 
-__global__ void __launch_bounds__(128) gdn_prep_kernel(const GdnPrep p) {
+__global__ void __launch_bounds__(128, 3) gdn_prep_kernel(const GdnPrep p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023) {
         if (threadIdx.x == 0) raise_status(STATUS_BAD_ARGUMENT);
