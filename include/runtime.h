@@ -121,6 +121,41 @@ int qv_delta(float *out, float *state, float *history,
              int batch, int key_heads, int value_heads, int dim,
              float epsilon, void *stream);
 
+/* Verify transaction of a DeltaNet layer, the state side of the reference's
+ * qv_verify / qv_commit (src/runtime.h:57-68; src/runtime.cu:363-374 saves the
+ * start state and history and records the transitions, src/runtime.cu:389-395
+ * with src/kernels.cu:356-360 writes the trace, src/runtime.cu:432-454 with
+ * src/kernels.cu:362-369, 567-574 commits).  All pointers are device memory,
+ * asynchronous on `stream`.
+ *
+ * qv_delta_verify is qv_delta (batch 1..8) that, in the same pass, copies the
+ * start state into saved_state [value_heads][dim][dim] and the start history
+ * into saved_history [3][C], and writes the transition trace into `trace`
+ * (qv_delta_trace_floats floats, C = (2*key_heads+value_heads)*dim): per
+ * token t < 8 the raw qkv row at t*C, the prepared row at (8+t)*C (q and k
+ * L2-normalised, q also times 1/sqrt(dim), v filtered), the decay at
+ * 16*C + t*value_heads + h and the beta at 16*C + 8*value_heads +
+ * t*value_heads + h.
+ *
+ * qv_delta_commit, after `accepted` of the `batch` verified tokens were kept
+ * (0 <= accepted <= batch): accepted == batch keeps the verify's result;
+ * otherwise state and history become the start state and history advanced
+ * by the first `accepted` tokens, rebuilt from the saved copies and the trace
+ * in one kernel (no start-state copy back). */
+size_t qv_delta_trace_floats(int key_heads, int value_heads, int dim);
+int qv_delta_verify(float *out, float *state, float *history,
+                    const float *qkv, const float *gate,
+                    const float *alpha, const float *beta,
+                    const float *conv, const float *decay,
+                    const float *bias, const float *norm,
+                    int batch, int key_heads, int value_heads, int dim,
+                    float epsilon, float *saved_state, float *saved_history,
+                    float *trace, void *stream);
+int qv_delta_commit(float *state, float *history, const float *saved_state,
+                    const float *saved_history, const float *trace,
+                    int accepted, int batch, int key_heads, int value_heads,
+                    int dim, void *stream);
+
 /* Sequence-split decode across GPUs.  A shard cache holds the absolute
  * positions [shard_begin, shard_begin+shard_rows) as rows [0,shard_rows).
  * When shard_begin+shard_rows == position the batch's new rows are appended

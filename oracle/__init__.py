@@ -11,6 +11,6 @@ were produced by running the reference oracle itself (``tests/golden/``), and
 by the reference's closed-form long-context known-answer test
 (``tests/test_cuda.py:237-273``), restated in ``oracle.closed_form``.
 """
-from .hotpath import (attention, delta, delta_core, prefill_attention_core,  # noqa: F401
-                      half, sigmoid, silu, softplus)
+from .hotpath import (attention, delta, delta_commit, delta_core, delta_trace,  # noqa: F401
+                      prefill_attention_core, half, sigmoid, silu, softplus)
 from . import inputs, closed_form  # noqa: F401

@@ -223,6 +223,77 @@ def delta(state, history, qkv, gate, alpha, beta, conv, decay, bias, norm,
     return out.reshape(-1), S.reshape(-1), hist.reshape(-1)
 
 
+
+def delta_trace(history, qkv, alpha, beta, conv, decay, bias, batch, key_heads, value_heads, dim):
+    """Transition trace of a recorded verify call, in the reference's layout.
+
+    The reference copies the raw qkv rows into the trace before the layer
+    (src/runtime.cu:389-390) and ``record_transition`` copies the prepared
+    rows and gates after conv and gdn_prep (src/kernels.cu:356-360, called at
+    src/kernels.cu:562): ``[8][C]`` raw rows, ``[8][C]`` prepared rows (q, k
+    L2-normalised with +1e-6, q times 1/sqrt(dim); v filtered; conv + SiLU as
+    cpu_reference.py:24-33), ``[8][Hv]`` decays ``exp(decay*softplus(alpha+bias))``
+    and ``[8][Hv]`` betas ``sigmoid(beta)`` (cpu_reference.py:37-38).  Rows of
+    tokens >= batch are left at zero.  Returns a float64 array of
+    ``8 * (2C + 2Hv)`` values.
+    """
+    C = (2 * key_heads + value_heads) * dim
+    hist = _as64(history).reshape(3, C).copy()
+    raw_all = _as64(qkv).reshape(batch, C)
+    al = _as64(alpha).reshape(batch, value_heads)
+    be = _as64(beta).reshape(batch, value_heads)
+    w = _as64(conv).reshape(C, 4)
+    dec, bi = _as64(decay), _as64(bias)
+    trace = np.zeros(8 * (2 * C + 2 * value_heads))
+    raw_t = trace[:8 * C].reshape(8, C)
+    prep_t = trace[8 * C:16 * C].reshape(8, C)
+    a_t = trace[16 * C:16 * C + 8 * value_heads].reshape(8, value_heads)
+    b_t = trace[16 * C + 8 * value_heads:].reshape(8, value_heads)
+    kd = key_heads * dim
+    for t in range(batch):
+        raw = raw_all[t]
+        filt = silu(((w[:, 0] * hist[0] + w[:, 1] * hist[1]) + w[:, 2] * hist[2]) + w[:, 3] * raw)
+        hist = np.concatenate([hist[1:], raw[None, :]], axis=0)
+        qs = filt[:kd].reshape(key_heads, dim)
+        ks = filt[kd:2 * kd].reshape(key_heads, dim)
+        raw_t[t] = raw
+        prep_t[t, :kd] = (qs / np.sqrt(np.sum(qs * qs, axis=1, keepdims=True) + 1e-6) / math.sqrt(dim)).reshape(-1)
+        prep_t[t, kd:2 * kd] = (ks / np.sqrt(np.sum(ks * ks, axis=1, keepdims=True) + 1e-6)).reshape(-1)
+        prep_t[t, 2 * kd:] = filt[2 * kd:]
+        a_t[t] = np.exp(dec * softplus(al[t] + bi))
+        b_t[t] = sigmoid(be[t])
+    return trace
+
+
+def delta_commit(saved_state, saved_history, trace, accepted, key_heads, value_heads, dim):
+    """State and conv history after committing ``accepted`` tokens of a
+    recorded verify (src/runtime.cu:432-454).
+
+    The start state and history are copied back, ``commit_history`` shifts the
+    accepted raw rows into the history window (src/kernels.cu:362-369), and
+    ``gdn_scan`` replays the accepted tokens' prepared rows and gates on the
+    state (src/kernels.cu:567-574; the row update of cpu_reference.py:40-45:
+    S *= a; S += outer(b (v - S k), k)).  Returns ``(state, history)`` float64.
+    """
+    C = (2 * key_heads + value_heads) * dim
+    S = _as64(saved_state).reshape(value_heads, dim, dim).copy()
+    hist = _as64(saved_history).reshape(3, C).copy()
+    tr = _as64(trace)
+    raw_t = tr[:8 * C].reshape(8, C)
+    prep_t = tr[8 * C:16 * C].reshape(8, C)
+    a_t = tr[16 * C:16 * C + 8 * value_heads].reshape(8, value_heads)
+    b_t = tr[16 * C + 8 * value_heads:].reshape(8, value_heads)
+    kd = key_heads * dim
+    for t in range(accepted):
+        hist = np.concatenate([hist[1:], raw_t[t][None, :]], axis=0)
+        ks = prep_t[t, kd:2 * kd].reshape(key_heads, dim)
+        vs = prep_t[t, 2 * kd:].reshape(value_heads, dim)
+        for h in range(value_heads):
+            k = ks[h % key_heads]
+            S[h] *= a_t[t, h]
+            S[h] += np.outer(b_t[t, h] * (vs[h] - S[h] @ k), k)
+    return S.reshape(-1), hist.reshape(-1)
+
 def delta_core(state, q, k, v, log_decay, beta):
     """The bare delta-rule recurrence on prepared inputs (cpu_reference.py:35-47).
 

@@ -27,9 +27,19 @@ struct DeltaArgs {
     const float *qkv, *gate, *alpha, *beta, *conv, *decay, *bias, *norm;
     // core mode (no conv / no gated norm): fp16 inputs
     const __half *q16, *k16, *v16;
+    // verify recording (layer mode, T <= 8): start state / history copies and
+    // the transition trace; null when not recording
+    float *saved_state, *saved_history, *trace;
     int T, Hk, Hv;
     float eps;
 };
+
+// Transition trace of one recorded verify call (the layout of the reference's
+// transitions buffer, src/runtime.cu:369 with src/kernels.cu:356-360): per
+// token t < 8, the raw qkv row [t][C], the prepared row [8 + t][C] (q and k
+// L2-normalised, q also scaled by 1/sqrt(D), v filtered), then the decays
+// [16 C + t Hv + h] and the betas [16 C + 8 Hv + t Hv + h].
+__host__ __device__ constexpr size_t delta_trace_floats(int C, int Hv) { return 8 * (2 * (size_t)C + 2 * (size_t)Hv); }
 
 // CORE = false: reference layer semantics (conv, SiLU, gated RMSNorm).
 // CORE = true : prepared-input recurrence (raw fp16 q/k/v are L2-normalised
@@ -102,6 +112,8 @@ delta_kernel(const DeltaArgs a) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (has_row) v = *reinterpret_cast<const float4 *>(srow + 32 * i + 4 * j);
         S[4 * i] = v.x; S[4 * i + 1] = v.y; S[4 * i + 2] = v.z; S[4 * i + 3] = v.w;
+        if (!CORE && a.saved_state && has_row)
+            *reinterpret_cast<float4 *>(a.saved_state + (srow - a.state) + 32 * i + 4 * j) = v;
     }
     // Conv channel of this thread: e < D -> q, e < 2D -> k, e < 2D + rows -> v row.
     const int e = tid;
@@ -114,6 +126,12 @@ delta_kernel(const DeltaArgs a) {
         const float4 w = *reinterpret_cast<const float4 *>(a.conv + (size_t)c * 4);
         w0 = w.x; w1 = w.y; w2 = w.z; w3 = w.w;
         h0 = a.history[c]; h1 = a.history[(size_t)C + c]; h2 = a.history[2 * (size_t)C + c];
+    }
+    // One CTA owns each channel's history (and trace) entries: v channels
+    // their rows' CTA, the q/k channels of key head kh rank 0 of value head kh.
+    const bool owns_channel = c >= 0 && (e >= 2 * D || (h < Hk && rank == 0));
+    if (!CORE && a.saved_history && owns_channel) {
+        a.saved_history[c] = h0; a.saved_history[(size_t)C + c] = h1; a.saved_history[2 * (size_t)C + c] = h2;
     }
     const float decay_h = a.decay[h], bias_h = a.bias[h];
     // Output of this thread in each chunk: token tid / rows, row tid % rows.
@@ -190,6 +208,23 @@ delta_kernel(const DeltaArgs a) {
             scal[tid][3] = sigmoidf_(be);
         }
         __syncthreads();
+        if (!CORE && a.trace) {
+            // transition trace (recorded calls have a single chunk)
+            if (owns_channel) {
+#pragma unroll
+                for (int tt = 0; tt < CHUNK; ++tt) {
+                    if (tt >= n) break;
+                    const float prep = e < D ? Fq[tt][e] * scal[tt][0]
+                                     : e < 2 * D ? Fk[tt][e - D] * scal[tt][1] : Fv[tt][e - 2 * D];
+                    a.trace[(size_t)tt * C + c] = raw[tt];
+                    a.trace[(size_t)(CHUNK + tt) * C + c] = prep;
+                }
+            }
+            if (rank == 0 && tid < n) {
+                a.trace[16 * (size_t)C + (size_t)tid * Hv + h] = scal[tid][2];
+                a.trace[16 * (size_t)C + 8 * (size_t)Hv + (size_t)tid * Hv + h] = scal[tid][3];
+            }
+        }
         // ---- delta rule over the chunk: S = a S; u = S k; delta = beta (v - u);
         //      S += delta k^T; o = S q   (k, q normalised through sk, sq).  The
         //      decay is applied inside the update: u = a (S k), S = a S + delta k.
@@ -268,8 +303,92 @@ delta_kernel(const DeltaArgs a) {
     }
     // History: v channels belong to their rows' CTA; the q/k channels of key
     // head kh are written by rank 0 of value head kh (h < Hk) only.
-    if (!CORE && c >= 0 && (e >= 2 * D || (h < Hk && rank == 0))) {
+    if (!CORE && owns_channel) {
         a.history[c] = h0; a.history[(size_t)C + c] = h1; a.history[2 * (size_t)C + c] = h2;
+    }
+}
+
+// Commit of a recorded verify call after `accepted` of its tokens were kept
+// (the reference's commit, src/runtime.cu:432-454: copy the start state and
+// history back, then k_delta_commit = commit_history + a state-only scan over
+// the accepted tokens, src/kernels.cu:362-369, 567-574).  Fused here into one
+// pass per (value head, row half): the start state is read once from its
+// saved copy, the accepted tokens' prepared rows and gates are replayed from
+// the trace, and the state and the conv history are written once.
+template <int D, int CPH>
+__global__ void __launch_bounds__(DeltaShape<D, CPH>::NT)
+delta_commit_kernel(float *state, float *history, const float *saved_state, const float *saved_history,
+                    const float *trace, int accepted, int Hk, int Hv) {
+    constexpr int MAXR = DeltaShape<D, CPH>::MAXR, NV4 = D / 32, COLS = D / 8;
+    const int rank = blockIdx.x % CPH, h = blockIdx.x / CPH, tid = threadIdx.x, kh = h % Hk;
+    const int C = (2 * Hk + Hv) * D;
+    const int row0 = rank * D / CPH, rows = (rank + 1) * D / CPH - row0;
+    const int r = tid >> 3, j = tid & 7;
+    const bool has_row = r < rows;
+    __shared__ __align__(16) float Fk[CHUNK][D], Fv[CHUNK][MAXR];
+    __shared__ float gat[CHUNK][2];                    // decay, beta
+    grid_dependency_wait();
+    if (tid == 0) launch_dependents();
+    const float *prep = trace + (size_t)CHUNK * C;
+    const float *decays = trace + 16 * (size_t)C, *betas = decays + 8 * (size_t)Hv;
+    for (int i = tid; i < accepted * D; i += blockDim.x)
+        Fk[i / D][i % D] = prep[(size_t)(i / D) * C + (Hk + kh) * D + i % D];
+    for (int i = tid; i < accepted * rows; i += blockDim.x)
+        Fv[i / rows][i % rows] = prep[(size_t)(i / rows) * C + (2 * Hk + h) * D + row0 + i % rows];
+    if (tid < accepted) {
+        gat[tid][0] = decays[(size_t)tid * Hv + h];
+        gat[tid][1] = betas[(size_t)tid * Hv + h];
+    }
+    float S[COLS];
+    const size_t srow = ((size_t)h * D + row0 + (has_row ? r : 0)) * D;
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has_row) v = *reinterpret_cast<const float4 *>(saved_state + srow + 32 * i + 4 * j);
+        S[4 * i] = v.x; S[4 * i + 1] = v.y; S[4 * i + 2] = v.z; S[4 * i + 3] = v.w;
+    }
+    __syncthreads();
+    // the reference row update per token: S = a S; delta = b (v - S k); S += delta k
+    for (int t = 0; t < accepted; ++t) {
+        const float decay = gat[t][0], beta = gat[t][1];
+        float4 k4[NV4];
+        float u0 = 0.f, u1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV4; ++i) {
+            k4[i] = *reinterpret_cast<const float4 *>(&Fk[t][32 * i + 4 * j]);
+            u0 += S[4 * i] * k4[i].x; u1 += S[4 * i + 1] * k4[i].y;
+            u0 += S[4 * i + 2] * k4[i].z; u1 += S[4 * i + 3] * k4[i].w;
+        }
+        float u = u0 + u1;
+        u += __shfl_xor_sync(0xffffffffu, u, 1);
+        u += __shfl_xor_sync(0xffffffffu, u, 2);
+        u += __shfl_xor_sync(0xffffffffu, u, 4);
+        const float delta = ((has_row ? Fv[t][r] : 0.f) - decay * u) * beta;
+#pragma unroll
+        for (int i = 0; i < NV4; ++i) {
+            S[4 * i] = fmaf(S[4 * i], decay, k4[i].x * delta);
+            S[4 * i + 1] = fmaf(S[4 * i + 1], decay, k4[i].y * delta);
+            S[4 * i + 2] = fmaf(S[4 * i + 2], decay, k4[i].z * delta);
+            S[4 * i + 3] = fmaf(S[4 * i + 3], decay, k4[i].w * delta);
+        }
+    }
+    if (has_row) {
+#pragma unroll
+        for (int i = 0; i < NV4; ++i)
+            *reinterpret_cast<float4 *>(state + srow + 32 * i + 4 * j) =
+                make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+    }
+    // conv history: the saved window shifted by the accepted raw rows (one
+    // owner per channel, as in the layer kernel)
+    const int e = tid;
+    int c = -1;
+    if (e < D) c = kh * D + e;
+    else if (e < 2 * D) c = (Hk + kh) * D + (e - D);
+    else if (e < 2 * D + rows) c = (2 * Hk + h) * D + row0 + (e - 2 * D);
+    if (c >= 0 && (e >= 2 * D || (h < Hk && rank == 0))) {
+        float w0 = saved_history[c], w1 = saved_history[(size_t)C + c], w2 = saved_history[2 * (size_t)C + c];
+        for (int t = 0; t < accepted; ++t) { w0 = w1; w1 = w2; w2 = trace[(size_t)t * C + c]; }
+        history[c] = w0; history[(size_t)C + c] = w1; history[2 * (size_t)C + c] = w2;
     }
 }
 
@@ -293,6 +412,39 @@ void delta_run(float *out, float *state, float *history, const float *qkv, const
     else if (D == 32) e = launch_chained(delta_kernel<32, 1, false>, dim3(Hv), dim3(DeltaShape<32, 1>::NT), 0, st, a);
     else throw std::invalid_argument("unsupported DeltaNet dimension");
     check_launch(e, "delta");
+}
+
+// Recorded verify: delta_run plus the start-state/history copies and the
+// transition trace (T <= 8).
+void delta_verify(float *out, float *state, float *history, const float *qkv, const float *gate,
+                  const float *alpha, const float *beta, const float *conv, const float *decay,
+                  const float *bias, const float *norm, int T, int Hk, int Hv, int D, float eps,
+                  float *saved_state, float *saved_history, float *trace, cudaStream_t st) {
+    if (T < 1 || T > CHUNK) throw std::invalid_argument("a recorded verify holds 1..8 tokens");
+    DeltaArgs a{};
+    a.out = out; a.state = state; a.history = history; a.qkv = qkv; a.gate = gate;
+    a.alpha = alpha; a.beta = beta; a.conv = conv; a.decay = decay; a.bias = bias; a.norm = norm;
+    a.saved_state = saved_state; a.saved_history = saved_history; a.trace = trace;
+    a.T = T; a.Hk = Hk; a.Hv = Hv; a.eps = eps;
+    cudaError_t e;
+    if (D == 128) e = launch_chained(delta_kernel<128, 2, false>, dim3(Hv * 2), dim3(DeltaShape<128, 2>::NT), 0, st, a);
+    else if (D == 32) e = launch_chained(delta_kernel<32, 1, false>, dim3(Hv), dim3(DeltaShape<32, 1>::NT), 0, st, a);
+    else throw std::invalid_argument("unsupported DeltaNet dimension");
+    check_launch(e, "delta verify");
+}
+
+void delta_commit(float *state, float *history, const float *saved_state, const float *saved_history,
+                  const float *trace, int accepted, int Hk, int Hv, int D, cudaStream_t st) {
+    if (accepted < 0 || accepted > CHUNK) throw std::invalid_argument("accepted must be between 0 and 8");
+    cudaError_t e;
+    if (D == 128)
+        e = launch_chained(delta_commit_kernel<128, 2>, dim3(Hv * 2), dim3(DeltaShape<128, 2>::NT), 0, st, state,
+                           history, saved_state, saved_history, trace, accepted, Hk, Hv);
+    else if (D == 32)
+        e = launch_chained(delta_commit_kernel<32, 1>, dim3(Hv), dim3(DeltaShape<32, 1>::NT), 0, st, state, history,
+                           saved_state, saved_history, trace, accepted, Hk, Hv);
+    else throw std::invalid_argument("unsupported DeltaNet dimension");
+    check_launch(e, "delta commit");
 }
 
 void delta_core_recurrent(float *out, float *state, const __half *q, const __half *k, const __half *v,

@@ -32,6 +32,15 @@ void delta_run(float *out, float *state, float *history, const float *qkv, const
                const float *alpha, const float *beta, const float *conv, const float *decay,
                const float *bias, const float *norm, int T, int Hk, int Hv, int D, float eps,
                cudaStream_t st);
+// Verify transaction: delta_run that also saves the start state / history and
+// writes the transition trace (8 (2C + 2Hv) floats, T <= 8); the commit
+// rebuilds state and history from those after `accepted` tokens were kept.
+void delta_verify(float *out, float *state, float *history, const float *qkv, const float *gate,
+                  const float *alpha, const float *beta, const float *conv, const float *decay,
+                  const float *bias, const float *norm, int T, int Hk, int Hv, int D, float eps,
+                  float *saved_state, float *saved_history, float *trace, cudaStream_t st);
+void delta_commit(float *state, float *history, const float *saved_state, const float *saved_history,
+                  const float *trace, int accepted, int Hk, int Hv, int D, cudaStream_t st);
 void delta_core_recurrent(float *out, float *state, const __half *q, const __half *k, const __half *v,
                           const float *alpha, const float *beta, const float *decay, const float *bias,
                           int T, int Hk, int Hv, int D, cudaStream_t st);

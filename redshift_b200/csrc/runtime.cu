@@ -327,6 +327,43 @@ int qv_delta(float *out, float *state, float *history, const float *qkv, const f
     });
 }
 
+size_t qv_delta_trace_floats(int key_heads, int value_heads, int dim) {
+    if (!(dim == 32 || dim == 128) || key_heads < 1 || value_heads < key_heads || value_heads > 48 ||
+        value_heads % key_heads != 0)
+        return 0;
+    return 8 * (2 * (size_t)(2 * key_heads + value_heads) * dim + 2 * (size_t)value_heads);
+}
+
+int qv_delta_verify(float *out, float *state, float *history, const float *qkv, const float *gate,
+                    const float *alpha, const float *beta, const float *conv, const float *decay,
+                    const float *bias, const float *norm, int batch, int key_heads, int value_heads, int dim,
+                    float epsilon, float *saved_state, float *saved_history, float *trace, void *stream) {
+    return guarded([&] {
+        require(batch >= 1 && batch <= 8, "a recorded verify holds 1..8 tokens");
+        check_epsilon(epsilon);
+        require(out && state && history && qkv && gate && alpha && beta && conv && decay && bias && norm,
+                "null DeltaNet buffer");
+        require(saved_state && saved_history && trace, "null verify record buffer");
+        check_delta_dims(key_heads, value_heads, dim);
+        qv::delta_verify(out, state, history, qkv, gate, alpha, beta, conv, decay, bias, norm, batch, key_heads,
+                         value_heads, dim, epsilon, saved_state, saved_history, trace, as_stream(stream));
+    });
+}
+
+int qv_delta_commit(float *state, float *history, const float *saved_state, const float *saved_history,
+                    const float *trace, int accepted, int batch, int key_heads, int value_heads, int dim,
+                    void *stream) {
+    return guarded([&] {
+        require(batch >= 1 && batch <= 8, "a recorded verify holds 1..8 tokens");
+        require(accepted >= 0 && accepted <= batch, "acceptance outside verified batch");
+        require(state && history && saved_state && saved_history && trace, "null commit buffer");
+        check_delta_dims(key_heads, value_heads, dim);
+        if (accepted == batch) return;          // the verify already left this state
+        qv::delta_commit(state, history, saved_state, saved_history, trace, accepted, key_heads, value_heads, dim,
+                         as_stream(stream));
+    });
+}
+
 size_t qv_attention_shard_workspace(int batch, int shard_rows) {
     if (batch < 1 || batch > qv::attention_max_shard_batch() || shard_rows < 0) return 0;
     // The split plan is not monotone in the row count: cover both cases.

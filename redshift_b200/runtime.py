@@ -44,6 +44,9 @@ ADDITIVE_SIGNATURES = {
     'qv_attention_workspace': ([_I, _I], _S),
     'qv_attention': ([_P] * 8 + [_I, _I, _F, _P, _S, _P], _I),
     'qv_delta': ([_P] * 11 + [_I] * 4 + [_F, _P], _I),
+    'qv_delta_trace_floats': ([_I, _I, _I], _S),
+    'qv_delta_verify': ([_P] * 11 + [_I] * 4 + [_F] + [_P] * 4, _I),
+    'qv_delta_commit': ([_P] * 5 + [_I] * 5 + [_P], _I),
     'qv_attention_shard_workspace': ([_I, _I], _S),
     'qv_attention_shard': ([_P] * 4 + [_I, _I] + [_P] * 5 + [_I, _I, _F, _P, _S, _P], _I),
     'qv_attention_merge': ([_P] * 3 + [_I, _I, _P, _P], _I),
@@ -171,6 +174,23 @@ class HotPath:
         self.check(self.lib.qv_delta(p(out), p(state), p(history), p(qkv), p(gate), p(alpha), p(beta),
                                      p(conv), p(decay), p(bias), p(norm), batch, key_heads, value_heads, dim,
                                      epsilon, self._stream()))
+
+    def delta_verify(self, out, state, history, qkv, gate, alpha, beta, conv, decay, bias, norm,
+                     batch, key_heads, value_heads, dim, saved_state, saved_history, trace, epsilon=1e-6):
+        """qv_delta_verify: qv_delta that also saves the start state / history and
+        writes the transition trace that qv_delta_commit replays."""
+        p = self._ptr
+        self.check(self.lib.qv_delta_verify(p(out), p(state), p(history), p(qkv), p(gate), p(alpha), p(beta),
+                                            p(conv), p(decay), p(bias), p(norm), batch, key_heads, value_heads,
+                                            dim, epsilon, p(saved_state), p(saved_history), p(trace),
+                                            self._stream()))
+
+    def delta_commit(self, state, history, saved_state, saved_history, trace, accepted, batch,
+                     key_heads, value_heads, dim):
+        """qv_delta_commit: keep the first `accepted` tokens of a recorded verify."""
+        p = self._ptr
+        self.check(self.lib.qv_delta_commit(p(state), p(history), p(saved_state), p(saved_history), p(trace),
+                                            accepted, batch, key_heads, value_heads, dim, self._stream()))
 
     def delta_core(self, out, state, q, k, v, alpha, beta, decay, bias, tokens, key_heads, value_heads, dim):
         p = self._ptr
