@@ -556,6 +556,47 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
     e1.record()
     torch.cuda.synchronize()
     res['delta_prefill_4096_recurrent_us'] = round(e0.elapsed_time(e1) * 1e3, 2)
+    del ws, qd, kd, vd, od
+    # verify/commit transaction: 48 DeltaNet layers with distinct states,
+    # plain layer vs recorded verify, and the commit of 3 of 8 tokens, each replayed as a graph
+    T8, C_ = 8, (2 * HK + HV) * DK
+    f32 = dict(device='cuda', dtype=torch.float32)
+    layers = [dict(state=torch.randn((HV, DK, DK), generator=g, **f32) * 0.02, history=torch.zeros((3, C_), **f32),
+                   saved_state=torch.empty((HV, DK, DK), **f32), saved_history=torch.empty((3, C_), **f32),
+                   trace=torch.empty(int(hot.lib.qv_delta_trace_floats(HK, HV, DK)), **f32)) for _ in range(48)]
+    conv = torch.zeros((C_, 4), **f32)
+    conv[:, 3] = 1
+    ins = (torch.randn((T8, C_), generator=g, **f32), torch.randn((T8, HV, DK), generator=g, **f32),
+           torch.randn((T8, HV), generator=g, **f32), torch.randn((T8, HV), generator=g, **f32), conv,
+           dec, bia, torch.ones(DK, **f32))
+    outd = torch.empty((T8, HV, DK), **f32)
+
+    def plain():
+        for d in layers:
+            hot.delta(outd, d['state'], d['history'], *ins, T8, HK, HV, DK)
+
+    def verify():
+        for d in layers:
+            hot.delta_verify(outd, d['state'], d['history'], *ins, T8, HK, HV, DK,
+                             d['saved_state'], d['saved_history'], d['trace'])
+
+    def commit():
+        for d in layers:
+            hot.delta_commit(d['state'], d['history'], d['saved_state'], d['saved_history'], d['trace'], 3, T8,
+                             HK, HV, DK)
+
+    for name, fn in (('delta_layer_us', plain), ('delta_verify_record_us', verify), ('delta_commit_3of8_us', commit)):
+        graph = capture(torch, fn)
+        for _ in range(3):
+            graph.replay()
+        e0.record()
+        for _ in range(5):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = round(e0.elapsed_time(e1) / (5 * 48) * 1e3, 2)
+        graph.reset()
+        del graph
     return res
 
 

@@ -67,9 +67,10 @@ template <int D, int CPH> struct DeltaShape {
     static constexpr int NT = ((MAXR * 8 + 31) / 32) * 32;         // threads per CTA
 };
 
-template <int D, int CPH, bool CORE>
+template <int D, int CPH, bool CORE, bool RECORD = false>
 __global__ void __cluster_dims__(CPH, 1, 1) __launch_bounds__(DeltaShape<D, CPH>::NT)
 delta_kernel(const DeltaArgs a) {
+    static_assert(!(CORE && RECORD), "only the layer mode records a verify");
     constexpr int MAXR = DeltaShape<D, CPH>::MAXR, NT = DeltaShape<D, CPH>::NT;
     constexpr int NV4 = D / 32, COLS = D / 8, NW = NT / 32;
     static_assert(2 * D + MAXR <= NT, "one conv channel per thread");
@@ -112,7 +113,7 @@ delta_kernel(const DeltaArgs a) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (has_row) v = *reinterpret_cast<const float4 *>(srow + 32 * i + 4 * j);
         S[4 * i] = v.x; S[4 * i + 1] = v.y; S[4 * i + 2] = v.z; S[4 * i + 3] = v.w;
-        if (!CORE && a.saved_state && has_row)
+        if (RECORD && has_row)
             *reinterpret_cast<float4 *>(a.saved_state + (srow - a.state) + 32 * i + 4 * j) = v;
     }
     // Conv channel of this thread: e < D -> q, e < 2D -> k, e < 2D + rows -> v row.
@@ -130,7 +131,7 @@ delta_kernel(const DeltaArgs a) {
     // One CTA owns each channel's history (and trace) entries: v channels
     // their rows' CTA, the q/k channels of key head kh rank 0 of value head kh.
     const bool owns_channel = c >= 0 && (e >= 2 * D || (h < Hk && rank == 0));
-    if (!CORE && a.saved_history && owns_channel) {
+    if (RECORD && owns_channel) {
         a.saved_history[c] = h0; a.saved_history[(size_t)C + c] = h1; a.saved_history[2 * (size_t)C + c] = h2;
     }
     const float decay_h = a.decay[h], bias_h = a.bias[h];
@@ -208,7 +209,7 @@ delta_kernel(const DeltaArgs a) {
             scal[tid][3] = sigmoidf_(be);
         }
         __syncthreads();
-        if (!CORE && a.trace) {
+        if (RECORD) {
             // transition trace (recorded calls have a single chunk)
             if (owns_channel) {
 #pragma unroll
@@ -303,7 +304,7 @@ delta_kernel(const DeltaArgs a) {
     }
     // History: v channels belong to their rows' CTA; the q/k channels of key
     // head kh are written by rank 0 of value head kh (h < Hk) only.
-    if (!CORE && owns_channel) {
+    if (!CORE && c >= 0 && (e >= 2 * D || (h < Hk && rank == 0))) {
         a.history[c] = h0; a.history[(size_t)C + c] = h1; a.history[2 * (size_t)C + c] = h2;
     }
 }
@@ -427,8 +428,10 @@ void delta_verify(float *out, float *state, float *history, const float *qkv, co
     a.saved_state = saved_state; a.saved_history = saved_history; a.trace = trace;
     a.T = T; a.Hk = Hk; a.Hv = Hv; a.eps = eps;
     cudaError_t e;
-    if (D == 128) e = launch_chained(delta_kernel<128, 2, false>, dim3(Hv * 2), dim3(DeltaShape<128, 2>::NT), 0, st, a);
-    else if (D == 32) e = launch_chained(delta_kernel<32, 1, false>, dim3(Hv), dim3(DeltaShape<32, 1>::NT), 0, st, a);
+    if (D == 128)
+        e = launch_chained(delta_kernel<128, 2, false, true>, dim3(Hv * 2), dim3(DeltaShape<128, 2>::NT), 0, st, a);
+    else if (D == 32)
+        e = launch_chained(delta_kernel<32, 1, false, true>, dim3(Hv), dim3(DeltaShape<32, 1>::NT), 0, st, a);
     else throw std::invalid_argument("unsupported DeltaNet dimension");
     check_launch(e, "delta verify");
 }
