@@ -45,6 +45,13 @@ void delta_core_recurrent(float *out, float *state, const __half *q, const __hal
                           const float *alpha, const float *beta, const float *decay, const float *bias,
                           int T, int Hk, int Hv, int D, cudaStream_t st);
 
+// Quantized projections (projection.cu): kinds 8 = Q8_0, 12 = Q4_K, 14 = Q6_K;
+// out [T][rows] = W [rows][width] x [T][width], T <= 8; `fast` = the 16-bit
+// activation-block path.
+size_t projection_weight_bytes(int kind, int width, int rows);
+void projection_run(float *out, const void *weights, const float *x, int kind, int T, int width, int rows,
+                    bool fast, cudaStream_t st);
+
 // Chunked gated DeltaNet prefill (gdn_chunk.cu): same inputs / outputs as
 // delta_core_recurrent, D = 128, chunks of 64 tokens on tcgen05.
 size_t delta_chunked_workspace_bytes(int T, int Hv);

@@ -1,0 +1,184 @@
+// Quantized projections for verify batches (T <= 8): out[t][row] = sum_k W[row][k] x[t][k]
+// with W in the GGUF block formats the reference model uses (src/kernels.cu:31-273,
+// 506-552; kinds 8 = Q8_0, 12 = Q4_K, 14 = Q6_K).
+//
+// Design (HBM-bound GEMV with a small batch):
+//  * a CTA of 8 warps owns 32 consecutive rows, 4 per warp; every activation
+//    value a lane loads from shared memory serves the warp's 4 rows;
+//  * the activations are staged in shared memory in chunks of 512 columns,
+//    token-major (conflict-free, coalesced), so any width fits;
+//  * within a chunk, lane l dequantises column 32 g + l of every 256-column
+//    super-block (every 32-column block for Q8_0): per (row, super-block) the
+//    header (scales, mins) is read once into registers, the quants are byte
+//    loads that are coalesced across the warp;
+//  * the 4 x 8 per-lane sums are reduced across the warp with a transposing
+//    butterfly (31 shuffles) that leaves sum v on lane v.
+// FAST = true is the reference's dp4a path semantics (runtime.h:17-20): the
+// activations are quantised per 32-column block to 16-bit integers (scale
+// max|x| / 32639, round half away from zero) and the weights' scale part
+// multiplies the quantised activations while the Q4_K minimum part multiplies
+// the exact activations (FP32 scales, sums and accumulation).
+#include "common.cuh"
+#include "hotpath.h"
+
+#include <stdexcept>
+#include <string>
+
+namespace qv {
+namespace {
+
+constexpr int QM_WARPS = 8, QM_RW = 4, QM_ROWS = QM_WARPS * QM_RW, QM_KC = 512, QM_T = 8;
+
+__device__ __forceinline__ float ld_half(const uint8_t *p) {
+    return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(p)));
+}
+
+// Q4_K 6-bit scale and minimum of group g (0..7) from the 12 packed bytes.
+__device__ __forceinline__ void q4k_scale_min(const uint8_t *sc, int g, float &s, float &z) {
+    if (g < 4) {
+        s = (float)(sc[g] & 63);
+        z = (float)(sc[g + 4] & 63);
+    } else {
+        s = (float)((sc[g + 4] & 15) | ((sc[g - 4] >> 6) << 4));
+        z = (float)((sc[g + 4] >> 4) | ((sc[g] >> 6) << 4));
+    }
+}
+
+template <int KIND, bool FAST>
+__global__ void __launch_bounds__(QM_WARPS * 32)
+qmm_kernel(float *out, const uint8_t *w, const float *x, int T, int width, int rows) {
+    constexpr int SB = KIND == 8 ? 32 : 256;                    // columns per block
+    constexpr int BB = KIND == 8 ? 34 : (KIND == 12 ? 144 : 210); // bytes per block
+    constexpr int G = SB / 32;                                   // 32-column groups per block
+    __shared__ float xs[QM_T][QM_KC];
+    __shared__ float qs[FAST ? QM_T : 1][FAST ? QM_KC : 1];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row0 = blockIdx.x * QM_ROWS + warp * QM_RW;
+    const size_t row_bytes = (size_t)(width / SB) * BB;
+    grid_dependency_wait();
+    if (tid == 0) launch_dependents();
+
+    float acc[QM_RW][QM_T];
+#pragma unroll
+    for (int r = 0; r < QM_RW; ++r)
+#pragma unroll
+        for (int t = 0; t < QM_T; ++t) acc[r][t] = 0.f;
+
+    for (int k0 = 0; k0 < width; k0 += QM_KC) {
+        const int len = min(QM_KC, width - k0);                  // a multiple of 32
+        __syncthreads();                                         // the previous chunk is consumed
+        for (int i = tid; i < QM_T * len; i += blockDim.x) {
+            const int t = i / len, kk = i % len;
+            xs[t][kk] = t < T ? x[(size_t)t * width + k0 + kk] : 0.f;
+        }
+        if (FAST) {
+            __syncthreads();
+            // 16-bit block quantisation of the activations: one warp per (token, 32-block)
+            for (int b = warp; b < QM_T * (len / 32); b += QM_WARPS) {
+                const int t = b / (len / 32), kk = (b % (len / 32)) * 32 + lane;
+                const float v = xs[t][kk];
+                float m = fabsf(v);
+#pragma unroll
+                for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                const float scale = m / 32639.f;
+                float q = 0.f;
+                if (scale != 0.f) {
+                    const float ratio = v / scale;
+                    q = copysignf(floorf(fabsf(ratio) + 0.5f), ratio);
+                }
+                qs[t][kk] = scale * q;
+            }
+        }
+        __syncthreads();
+        for (int sb = 0; sb < len / SB; ++sb) {
+            const int blk = k0 / SB + sb;
+            // per-row block base pointers (rows past the end are skipped uniformly)
+            const uint8_t *base[QM_RW];
+#pragma unroll
+            for (int r = 0; r < QM_RW; ++r)
+                base[r] = w + (size_t)min(row0 + r, rows - 1) * row_bytes + (size_t)blk * BB;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const int kk = sb * SB + g * 32 + lane;
+                float xv[QM_T], qv[QM_T];
+#pragma unroll
+                for (int t = 0; t < QM_T; ++t) {
+                    xv[t] = xs[t][kk];
+                    qv[t] = FAST ? qs[FAST ? t : 0][FAST ? kk : 0] : 0.f;
+                }
+#pragma unroll
+                for (int r = 0; r < QM_RW; ++r) {
+                    if (row0 + r >= rows) continue;
+                    const uint8_t *b = base[r];
+                    float wq, off = 0.f;                          // weight = wq - off
+                    if (KIND == 8) {
+                        wq = ld_half(b) * (float)(int8_t)b[2 + lane];
+                    } else if (KIND == 12) {
+                        float s, z;
+                        q4k_scale_min(b + 4, g, s, z);
+                        const int q = (b[16 + (g >> 1) * 32 + lane] >> (4 * (g & 1))) & 15;
+                        wq = ld_half(b) * s * (float)q;
+                        off = ld_half(b + 2) * z;
+                    } else {
+                        const int half = g >> 2, quarter = g & 3;
+                        const int low = (b[half * 64 + (quarter & 1) * 32 + lane] >> (4 * (quarter >> 1))) & 15;
+                        const int high = (b[128 + half * 32 + lane] >> (2 * quarter)) & 3;
+                        const int sc = (int8_t)b[192 + g * 2 + (lane >> 4)];
+                        wq = (float)(high * 16 + low - 32) * (float)sc * ld_half(b + 208);
+                    }
+#pragma unroll
+                    for (int t = 0; t < QM_T; ++t) {
+                        if (FAST) acc[r][t] = fmaf(wq, qv[t], fmaf(-off, xv[t], acc[r][t]));
+                        else acc[r][t] = fmaf(wq - off, xv[t], acc[r][t]);
+                    }
+                }
+            }
+        }
+    }
+    // transposing butterfly: lane l ends with the sum of value l = r * 8 + t
+    float v[QM_RW * QM_T];
+#pragma unroll
+    for (int r = 0; r < QM_RW; ++r)
+#pragma unroll
+        for (int t = 0; t < QM_T; ++t) v[r * QM_T + t] = acc[r][t];
+#pragma unroll
+    for (int half = 16; half >= 1; half >>= 1) {
+        const bool up = (lane & half) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float lo = v[i], hi = v[i + half];
+            v[i] = (up ? hi : lo) + __shfl_xor_sync(0xffffffffu, up ? lo : hi, half);
+        }
+    }
+    const int r = lane / QM_T, t = lane % QM_T, row = row0 + r;
+    if (row < rows && t < T) out[(size_t)t * rows + row] = v[0];
+}
+
+template <int KIND>
+cudaError_t launch_kind(float *out, const uint8_t *w, const float *x, int T, int width, int rows, bool fast,
+                        cudaStream_t st) {
+    const dim3 grid((rows + QM_ROWS - 1) / QM_ROWS), block(QM_WARPS * 32);
+    return fast ? launch_chained(qmm_kernel<KIND, true>, grid, block, 0, st, out, w, x, T, width, rows)
+                : launch_chained(qmm_kernel<KIND, false>, grid, block, 0, st, out, w, x, T, width, rows);
+}
+
+}  // namespace
+
+size_t projection_weight_bytes(int kind, int width, int rows) {
+    const int sb = kind == 8 ? 32 : 256, bb = kind == 8 ? 34 : (kind == 12 ? 144 : 210);
+    return (size_t)(width / sb) * bb * rows;
+}
+
+void projection_run(float *out, const void *weights, const float *x, int kind, int T, int width, int rows,
+                    bool fast, cudaStream_t st) {
+    if (T < 1 || T > QM_T) throw std::invalid_argument("projection batch must be between 1 and 8");
+    const uint8_t *w = static_cast<const uint8_t *>(weights);
+    cudaError_t e;
+    if (kind == 8) e = launch_kind<8>(out, w, x, T, width, rows, fast, st);
+    else if (kind == 12) e = launch_kind<12>(out, w, x, T, width, rows, fast, st);
+    else if (kind == 14) e = launch_kind<14>(out, w, x, T, width, rows, fast, st);
+    else throw std::invalid_argument("unsupported quantization type");
+    if (e != cudaSuccess) throw std::runtime_error(std::string("projection: ") + cudaGetErrorString(e));
+}
+
+}  // namespace qv

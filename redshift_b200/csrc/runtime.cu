@@ -194,22 +194,31 @@ extern "C" {
 const char *qv_error(void) { return g_message; }
 
 // ------------------------------------------------------------------ projections
-static int projection_unsupported(float *out, const void *weights, const float *x, int kind, int batch,
-                                  int width, int rows) {
+// Quantized projection through host buffers (the reference's test_projection,
+// src/runtime.cu:80-113): allocate, upload, run, download, synchronously.
+static int test_projection(float *out, const void *weights, const float *x, int kind, int batch, int width,
+                           int rows, bool fast) {
     return guarded([&] {
         require(batch >= 1 && batch <= 8, "batch must be between 1 and 8");
         require(out && weights && x, "null projection buffer");
         require(kind == 8 || kind == 12 || kind == 14, "unsupported quantization type");
         const int block = kind == 8 ? 32 : 256;
         require(width > 0 && width % block == 0 && rows > 0 && rows <= 248320, "invalid projection dimensions");
-        throw Failure("quantized projections are not part of this build");
+        const size_t wbytes = qv::projection_weight_bytes(kind, width, rows);
+        const size_t xbytes = (size_t)batch * width * sizeof(float), obytes = (size_t)batch * rows * sizeof(float);
+        DeviceBuffer w(wbytes), in(xbytes), o(obytes);
+        w.upload(weights, wbytes);
+        in.upload(x, xbytes);
+        qv::projection_run(o.get<float>(), w.get(), in.get<float>(), kind, batch, width, rows, fast, nullptr);
+        finish();
+        o.download(out, obytes);
     });
 }
 int qv_test_mm(float *out, const void *weights, const float *x, int kind, int batch, int width, int rows) {
-    return projection_unsupported(out, weights, x, kind, batch, width, rows);
+    return test_projection(out, weights, x, kind, batch, width, rows, false);
 }
 int qv_test_mm_fast(float *out, const void *weights, const float *x, int kind, int batch, int width, int rows) {
-    return projection_unsupported(out, weights, x, kind, batch, width, rows);
+    return test_projection(out, weights, x, kind, batch, width, rows, true);
 }
 
 int qv_test_norm(float *out, const float *x, const float *weights, int batch, int width, float epsilon) {

@@ -93,12 +93,6 @@ def test_rejects_invalid_arguments_before_accessing_buffers(lib):
     assert lib.qv_test_delta_prefill(*([value] * 11), 0, 1, 1, 32, 1e-6) == -1
 
 
-def test_projections_are_reported_out_of_build(lib):
-    value = floats([1.])
-    assert lib.qv_test_mm(value, value, value, 8, 1, 32, 1) == -1
-    assert b'not part of this build' in lib.qv_error()
-
-
 def test_model_abi_fails_cleanly(lib):
     handle = ct.c_void_p()
     assert lib.qv_create(None, b'x', 16, 1e-6) == -1
