@@ -597,6 +597,36 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
         res[name] = round(e0.elapsed_time(e1) / (5 * 48) * 1e3, 2)
         graph.reset()
         del graph
+    del layers
+    # quantized projections: verify batch of 8 through a 17408 x 5120
+    # matrix (the model's FFN shape), four distinct matrices in rotation (> L2)
+    for kind, name in ((8, 'q8_0'), (12, 'q4_k'), (14, 'q6_k')):
+        wbytes = int(hot.lib.qv_mm_weight_bytes(kind, 5120, 17408))
+        mats = [torch.randint(0, 256, (wbytes,), generator=g, device='cuda', dtype=torch.uint8) for _ in range(4)]
+        for m_ in mats:                     # finite fp16 block scales (first header bytes of each block)
+            blk = 34 if kind == 8 else (144 if kind == 12 else 210)
+            v = m_.view(-1, blk)
+            scale = torch.tensor([0x00, 0x20] if kind != 14 else [0x00, 0x1c], dtype=torch.uint8, device='cuda')
+            if kind == 14:
+                v[:, 208:210] = scale
+            else:
+                v[:, 0:2] = scale
+                if kind == 12:
+                    v[:, 2:4] = scale
+        xq = torch.randn((8, 5120), generator=g, device='cuda')
+        oq = torch.empty((8, 17408), device='cuda')
+        for _ in range(3):
+            hot.mm(oq, mats[0], xq, kind, 8, 5120, 17408)
+        e0.record()
+        for i in range(20):
+            hot.mm(oq, mats[i % 4], xq, kind, 8, 5120, 17408)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 20
+        byt = wbytes + 8 * 5120 * 4 + 8 * 17408 * 4
+        res[f'mm_{name}_17408x5120_t8_us'] = round(ms * 1e3, 2)
+        res[f'mm_{name}_hbm_frac'] = round(byt / (ms * 1e-3) / 1e9 / hbm_peak, 4)
+        del mats
     return res
 
 

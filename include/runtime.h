@@ -23,10 +23,12 @@ extern "C" {
 /* Replaces src/runtime.h:14 (thread-local message of the last failure). */
 const char *qv_error(void);
 
-/* Replace src/runtime.h:15-21.  Quantized projections are outside this
- * build's hot path: arguments are validated exactly like the reference
- * (kind 8/12/14, batch 1..8, width multiple of the block, 1..248320 rows),
- * then the call fails with "quantized projections are not part of this build". */
+/* Replace src/runtime.h:15-21 (the reference's test_projection,
+ * src/runtime.cu:80-113).  out [batch][rows] = W x for W [rows][width] in
+ * block format kind 8 (Q8_0), 12 (Q4_K) or 14 (Q6_K), batch 1..8, width a
+ * multiple of the block (32 / 256), 1..248320 rows; host buffers,
+ * synchronous.  qv_test_mm_fast quantises the activations per 32-column block
+ * to 16-bit integers first (the reference's dp4a path semantics). */
 int qv_test_mm(float *out, const void *weights, const float *x,
                int kind, int batch, int width, int rows);
 int qv_test_mm_fast(float *out, const void *weights, const float *x,
@@ -64,7 +66,7 @@ int qv_test_attention(float *out, void *key_cache, void *value_cache,
                       int batch, int position, float epsilon);
 
 /* Replace src/runtime.h:54-74.  Full-model evaluation needs the quantized
- * projections and the GGUF loader, which are outside this build: qv_create
+ * weights of the GGUF file and its loader, which are outside this build: qv_create
  * validates its arguments then fails; every call on a handle fails with
  * "null model handle"; qv_destroy(NULL) is a no-op. */
 int qv_create(void **handle, const char *path, int context, float epsilon);
@@ -120,6 +122,16 @@ int qv_delta(float *out, float *state, float *history,
              const float *bias, const float *norm,
              int batch, int key_heads, int value_heads, int dim,
              float epsilon, void *stream);
+
+/* Device-resident quantized projection: the operation the reference model's
+ * projection() performs (src/runtime.cu:345-354 with src/kernels.cu:506-552):
+ * out [batch][rows] = W x for batch 1..8, W [rows][width] in block format
+ * `kind` (8 = Q8_0, 12 = Q4_K, 14 = Q6_K; qv_mm_weight_bytes bytes), x
+ * [batch][width] f32.  fast != 0 selects the 16-bit activation-block path of
+ * qv_test_mm_fast.  All pointers are device memory; asynchronous on `stream`. */
+size_t qv_mm_weight_bytes(int kind, int width, int rows);
+int qv_mm(float *out, const void *weights, const float *x, int kind, int batch,
+          int width, int rows, int fast, void *stream);
 
 /* Verify transaction of a DeltaNet layer, the state side of the reference's
  * qv_verify / qv_commit (src/runtime.h:57-68; src/runtime.cu:363-374 saves the

@@ -260,7 +260,7 @@ int qv_create(void **handle, const char *path, int context, float epsilon) {
         require(path != nullptr, "null model path");
         require(context >= 1 && context <= kMaxContext, "context capacity must be 1..139264");
         check_epsilon(epsilon);
-        throw Failure("full-model evaluation (GGUF weights, quantized projections) is not part of this build");
+        throw Failure("full-model evaluation (GGUF weights and loader) is not part of this build");
     });
 }
 static int no_model(void *handle) {
@@ -333,6 +333,24 @@ int qv_delta(float *out, float *state, float *history, const float *qkv, const f
         check_delta_dims(key_heads, value_heads, dim);
         qv::delta_run(out, state, history, qkv, gate, alpha, beta, conv, decay, bias, norm, batch, key_heads,
                       value_heads, dim, epsilon, as_stream(stream));
+    });
+}
+
+size_t qv_mm_weight_bytes(int kind, int width, int rows) {
+    if (!(kind == 8 || kind == 12 || kind == 14) || width <= 0 || rows <= 0 || width % (kind == 8 ? 32 : 256))
+        return 0;
+    return qv::projection_weight_bytes(kind, width, rows);
+}
+
+int qv_mm(float *out, const void *weights, const float *x, int kind, int batch, int width, int rows, int fast,
+          void *stream) {
+    return guarded([&] {
+        require(batch >= 1 && batch <= 8, "batch must be between 1 and 8");
+        require(out && weights && x, "null projection buffer");
+        require(kind == 8 || kind == 12 || kind == 14, "unsupported quantization type");
+        const int block = kind == 8 ? 32 : 256;
+        require(width > 0 && width % block == 0 && rows > 0 && rows <= 248320, "invalid projection dimensions");
+        qv::projection_run(out, weights, x, kind, batch, width, rows, fast != 0, as_stream(stream));
     });
 }
 

@@ -45,6 +45,8 @@ ADDITIVE_SIGNATURES = {
     'qv_attention': ([_P] * 8 + [_I, _I, _F, _P, _S, _P], _I),
     'qv_delta': ([_P] * 11 + [_I] * 4 + [_F, _P], _I),
     'qv_delta_trace_floats': ([_I, _I, _I], _S),
+    'qv_mm_weight_bytes': ([_I, _I, _I], _S),
+    'qv_mm': ([_P] * 3 + [_I] * 5 + [_P], _I),
     'qv_delta_verify': ([_P] * 11 + [_I] * 4 + [_F] + [_P] * 4, _I),
     'qv_delta_commit': ([_P] * 5 + [_I] * 5 + [_P], _I),
     'qv_attention_shard_workspace': ([_I, _I], _S),
@@ -174,6 +176,12 @@ class HotPath:
         self.check(self.lib.qv_delta(p(out), p(state), p(history), p(qkv), p(gate), p(alpha), p(beta),
                                      p(conv), p(decay), p(bias), p(norm), batch, key_heads, value_heads, dim,
                                      epsilon, self._stream()))
+
+    def mm(self, out, weights, x, kind, batch, width, rows, fast=False):
+        """qv_mm: out [batch][rows] = W x for a block-quantized W on the device."""
+        p = self._ptr
+        self.check(self.lib.qv_mm(p(out), p(weights), p(x), kind, batch, width, rows, int(bool(fast)),
+                                  self._stream()))
 
     def delta_verify(self, out, state, history, qkv, gate, alpha, beta, conv, decay, bias, norm,
                      batch, key_heads, value_heads, dim, saved_state, saved_history, trace, epsilon=1e-6):

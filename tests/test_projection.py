@@ -113,3 +113,21 @@ def test_model_width_and_ragged_rows(lib, kind):
     # ten times the reference test's width: the FP32 accumulation error of a
     # 5120-term sum with cancellation exceeds the 2e-5 of the 512-wide case
     _close(_run(lib, lib.qv_test_mm, data, x, kind, batch, width, rows), P.mm(kind, data, x, batch, width, rows), 1e-4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize('kind', [8, 12, 14])
+def test_device_entry_matches_host_entry(lib, hot, kind):
+    import torch
+    width, rows, batch = 768, 67, 5
+    data = make_weights(kind, width, rows, 11)
+    x = activations(batch, width, outliers=True)
+    assert lib.qv_mm_weight_bytes(kind, width, rows) == len(data)
+    w = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
+    xd = torch.from_numpy(x).cuda()
+    for fast, fn in ((False, lib.qv_test_mm), (True, lib.qv_test_mm_fast)):
+        out = torch.empty((batch, rows), device='cuda')
+        hot.mm(out, w, xd, kind, batch, width, rows, fast=fast)
+        torch.cuda.synchronize()
+        host = _run(lib, fn, data, x, kind, batch, width, rows)
+        np.testing.assert_array_equal(out.cpu().numpy().astype(np.float64), host)
