@@ -5,12 +5,14 @@
 // Design (HBM-bound GEMV with a small batch):
 //  * a CTA of 8 warps owns 32 consecutive rows, 4 per warp; every activation
 //    value a lane loads from shared memory serves the warp's 4 rows;
-//  * the activations are staged in shared memory in chunks of 512 columns,
-//    token-major (conflict-free, coalesced), so any width fits;
-//  * within a chunk, lane l dequantises column 32 g + l of every 256-column
-//    super-block (every 32-column block for Q8_0): per (row, super-block) the
-//    header (scales, mins) is read once into registers, the quants are byte
-//    loads that are coalesced across the warp;
+//  * the columns are processed in chunks of 256: the activations of a chunk
+//    are staged in shared memory token-major (conflict-free, coalesced), and
+//    the chunk's block bytes of the CTA's 32 rows are staged next to them with
+//    coalesced, independent 16-bit loads (every block size and row length is
+//    even, so 2-byte alignment is all the formats guarantee), unrolled so
+//    that many loads are in flight per thread;
+//  * lane l then dequantises column 32 g + l of every block from shared
+//    memory;
 //  * the 4 x 8 per-lane sums are reduced across the warp with a transposing
 //    butterfly (31 shuffles) that leaves sum v on lane v.
 // FAST = true is the reference's dp4a path semantics (runtime.h:17-20): the
@@ -27,7 +29,7 @@
 namespace qv {
 namespace {
 
-constexpr int QM_WARPS = 8, QM_RW = 4, QM_ROWS = QM_WARPS * QM_RW, QM_KC = 512, QM_T = 8;
+constexpr int QM_WARPS = 8, QM_RW = 4, QM_ROWS = QM_WARPS * QM_RW, QM_KC = 256, QM_T = 8;
 
 __device__ __forceinline__ float ld_half(const uint8_t *p) {
     return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(p)));
@@ -50,8 +52,10 @@ qmm_kernel(float *out, const uint8_t *w, const float *x, int T, int width, int r
     constexpr int SB = KIND == 8 ? 32 : 256;                    // columns per block
     constexpr int BB = KIND == 8 ? 34 : (KIND == 12 ? 144 : 210); // bytes per block
     constexpr int G = SB / 32;                                   // 32-column groups per block
+    constexpr int CB = (QM_KC / SB) * BB;                        // bytes of one row in a full chunk
     __shared__ float xs[QM_T][QM_KC];
     __shared__ float qs[FAST ? QM_T : 1][FAST ? QM_KC : 1];
+    __shared__ __align__(16) uint16_t wbuf[QM_ROWS * CB / 2];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row0 = blockIdx.x * QM_ROWS + warp * QM_RW;
     const size_t row_bytes = (size_t)(width / SB) * BB;
@@ -67,9 +71,24 @@ qmm_kernel(float *out, const uint8_t *w, const float *x, int T, int width, int r
     for (int k0 = 0; k0 < width; k0 += QM_KC) {
         const int len = min(QM_KC, width - k0);                  // a multiple of 32
         __syncthreads();                                         // the previous chunk is consumed
-        for (int i = tid; i < QM_T * len; i += blockDim.x) {
-            const int t = i / len, kk = i % len;
-            xs[t][kk] = t < T ? x[(size_t)t * width + k0 + kk] : 0.f;
+#pragma unroll
+        for (int t = 0; t < QM_T; ++t)
+            for (int kk = tid; kk < len; kk += QM_WARPS * 32)
+                xs[t][kk] = t < T ? x[(size_t)t * width + k0 + kk] : 0.f;
+        {
+            // the chunk's 16-bit words of the CTA's rows; divisions by the
+            // compile-time row stride, a partial last chunk (Q8_0 only) masked
+            constexpr int HW = CB / 2;
+            const int half_words = (len / SB) * BB / 2;
+            const size_t col_off = (size_t)(k0 / SB) * BB;
+            const uint8_t *rows0 = w + (size_t)blockIdx.x * QM_ROWS * row_bytes + col_off;
+            const int nrows = min(QM_ROWS, rows - (int)blockIdx.x * QM_ROWS);
+#pragma unroll 4
+            for (int i = tid; i < QM_ROWS * HW; i += QM_WARPS * 32) {
+                const int r = i / HW, j = i - r * HW;
+                wbuf[i] = (r < nrows && j < half_words)
+                              ? reinterpret_cast<const uint16_t *>(rows0 + (size_t)r * row_bytes)[j] : 0;
+            }
         }
         if (FAST) {
             __syncthreads();
@@ -90,13 +109,12 @@ qmm_kernel(float *out, const uint8_t *w, const float *x, int T, int width, int r
             }
         }
         __syncthreads();
+        const uint8_t *wb = reinterpret_cast<const uint8_t *>(wbuf);
         for (int sb = 0; sb < len / SB; ++sb) {
-            const int blk = k0 / SB + sb;
-            // per-row block base pointers (rows past the end are skipped uniformly)
+            // block base pointers of the warp's rows in the staged chunk
             const uint8_t *base[QM_RW];
 #pragma unroll
-            for (int r = 0; r < QM_RW; ++r)
-                base[r] = w + (size_t)min(row0 + r, rows - 1) * row_bytes + (size_t)blk * BB;
+            for (int r = 0; r < QM_RW; ++r) base[r] = wb + (warp * QM_RW + r) * CB + sb * BB;
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const int kk = sb * SB + g * 32 + lane;

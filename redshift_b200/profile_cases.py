@@ -6,6 +6,7 @@
     python -m redshift_b200.profile_cases prefill [tokens]    # core causal prefill attention
     python -m redshift_b200.profile_cases delta_core [tokens] # DeltaNet prefill recurrence (core)
     python -m redshift_b200.profile_cases delta_chunked [tokens] # DeltaNet prefill, chunked tcgen05 form
+    python -m redshift_b200.profile_cases mm_q8_0 [rows]      # verify-8 projection, width 5120 (also mm_q4_k, mm_q6_k)
 
 Options: ``--reps N`` launches (default 3), ``--time`` prints the mean
 CUDA-event time of the last N launches.  Inputs are seeded N(0,1) (DeltaNet
@@ -82,6 +83,25 @@ def make_case(hot, case, size):
             ws = torch.empty(hot.lib.qv_delta_chunked_workspace(T, HV), dtype=torch.uint8, device=dev)
             return lambda: hot.delta_chunked(out, state, q, k, v, alpha, beta, decay, bias, T, HK, HV, DK, workspace=ws)
         return lambda: hot.delta_core(out, state, q, k, v, alpha, beta, decay, bias, T, HK, HV, DK)
+    if case.startswith('mm_'):
+        kind = {'mm_q8_0': 8, 'mm_q4_k': 12, 'mm_q6_k': 14}[case]
+        T, width, rows = 8, 5120, size or 17408
+        nbytes = int(hot.lib.qv_mm_weight_bytes(kind, width, rows))
+        blk = 34 if kind == 8 else (144 if kind == 12 else 210)
+        w = torch.randint(0, 256, (nbytes,), generator=g, device=dev, dtype=torch.uint8)
+        v = w.view(-1, blk)                 # finite fp16 block scales: 2^-7 (Q8_0, Q4_K d and dmin), 2^-8 (Q6_K)
+        if kind == 14:
+            v[:, 208] = 0x00
+            v[:, 209] = 0x1c
+        else:
+            v[:, 0] = 0x00
+            v[:, 1] = 0x20
+            if kind == 12:
+                v[:, 2] = 0x00
+                v[:, 3] = 0x20
+        x = torch.randn((T, width), generator=g, **f32)
+        out = torch.empty((T, rows), **f32)
+        return lambda: hot.mm(out, w, x, kind, T, width, rows)
     if case == 'prefill':
         L = size or 4096
         q = torch.randn((L, H, HD), generator=g, device=dev, dtype=torch.float16)
@@ -94,7 +114,8 @@ def make_case(hot, case, size):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument('case', choices=['decode', 'decode_exchange', 'delta', 'prefill', 'delta_core', 'delta_chunked'])
+    ap.add_argument('case', choices=['decode', 'decode_exchange', 'delta', 'prefill', 'delta_core', 'delta_chunked',
+                                     'mm_q8_0', 'mm_q4_k', 'mm_q6_k'])
     ap.add_argument('size', type=int, nargs='?', default=0)
     ap.add_argument('--reps', type=int, default=3)
     ap.add_argument('--time', action='store_true')
