@@ -11,8 +11,10 @@
 //    coalesced, independent 16-bit loads (every block size and row length is
 //    even, so 2-byte alignment is all the formats guarantee), unrolled so
 //    that many loads are in flight per thread;
-//  * lane l then dequantises column 32 g + l of every block from shared
-//    memory;
+//  * lane l then takes 4 consecutive columns of a 32-column group (8 lanes
+//    per group, 4 groups per step): one 32-bit load of its quants per row,
+//    the group's scale decoded once for the 4 columns, one 128-bit load of
+//    the activations per token shared by the warp's 4 rows;
 //  * the 4 x 8 per-lane sums are reduced across the warp with a transposing
 //    butterfly (31 shuffles) that leaves sum v on lane v.
 // FAST = true is the reference's dp4a path semantics (runtime.h:17-20): the
@@ -35,27 +37,16 @@ __device__ __forceinline__ float ld_half(const uint8_t *p) {
     return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(p)));
 }
 
-// Q4_K 6-bit scale and minimum of group g (0..7) from the 12 packed bytes.
-__device__ __forceinline__ void q4k_scale_min(const uint8_t *sc, int g, float &s, float &z) {
-    if (g < 4) {
-        s = (float)(sc[g] & 63);
-        z = (float)(sc[g + 4] & 63);
-    } else {
-        s = (float)((sc[g + 4] & 15) | ((sc[g - 4] >> 6) << 4));
-        z = (float)((sc[g + 4] >> 4) | ((sc[g] >> 6) << 4));
-    }
-}
-
 template <int KIND, bool FAST>
 __global__ void __launch_bounds__(QM_WARPS * 32)
 qmm_kernel(float *out, const uint8_t *w, const float *x, int T, int width, int rows) {
     constexpr int SB = KIND == 8 ? 32 : 256;                    // columns per block
     constexpr int BB = KIND == 8 ? 34 : (KIND == 12 ? 144 : 210); // bytes per block
-    constexpr int G = SB / 32;                                   // 32-column groups per block
     constexpr int CB = (QM_KC / SB) * BB;                        // bytes of one row in a full chunk
-    __shared__ float xs[QM_T][QM_KC];
-    __shared__ float qs[FAST ? QM_T : 1][FAST ? QM_KC : 1];
-    __shared__ __align__(16) uint16_t wbuf[QM_ROWS * CB / 2];
+    constexpr int CBP = (CB + 15) / 16 * 16;                     // its shared-memory stride (16-byte rows)
+    __shared__ __align__(16) float xs[QM_T][QM_KC];
+    __shared__ __align__(16) float qs[FAST ? QM_T : 1][FAST ? QM_KC : 4];
+    __shared__ __align__(16) uint16_t wbuf[QM_ROWS * CBP / 2];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row0 = blockIdx.x * QM_ROWS + warp * QM_RW;
     const size_t row_bytes = (size_t)(width / SB) * BB;
@@ -86,7 +77,7 @@ qmm_kernel(float *out, const uint8_t *w, const float *x, int T, int width, int r
 #pragma unroll 4
             for (int i = tid; i < QM_ROWS * HW; i += QM_WARPS * 32) {
                 const int r = i / HW, j = i - r * HW;
-                wbuf[i] = (r < nrows && j < half_words)
+                wbuf[r * (CBP / 2) + j] = (r < nrows && j < half_words)
                               ? reinterpret_cast<const uint16_t *>(rows0 + (size_t)r * row_bytes)[j] : 0;
             }
         }
@@ -110,45 +101,65 @@ qmm_kernel(float *out, const uint8_t *w, const float *x, int T, int width, int r
         }
         __syncthreads();
         const uint8_t *wb = reinterpret_cast<const uint8_t *>(wbuf);
-        for (int sb = 0; sb < len / SB; ++sb) {
-            // block base pointers of the warp's rows in the staged chunk
-            const uint8_t *base[QM_RW];
+        // lane l covers 4 consecutive columns of a 32-column group: group
+        // 4 step + l / 8 of the chunk, columns 4 (l % 8) .. + 3 within it
+        const int lg = lane >> 3, lc = (lane & 7) * 4;
+        for (int step = 0; step * 128 < len; ++step) {
+            const int c = step * 128 + lg * 32 + lc;             // first column (within the chunk)
+            if (c >= len) continue;                              // a partial Q8_0 chunk
+            float4 x4[QM_T], q4[QM_T];
+            float xsum[QM_T];
 #pragma unroll
-            for (int r = 0; r < QM_RW; ++r) base[r] = wb + (warp * QM_RW + r) * CB + sb * BB;
+            for (int t = 0; t < QM_T; ++t) {
+                x4[t] = *reinterpret_cast<const float4 *>(&xs[t][c]);
+                q4[t] = FAST ? *reinterpret_cast<const float4 *>(&qs[FAST ? t : 0][FAST ? c : 0]) : x4[t];
+                xsum[t] = (x4[t].x + x4[t].y) + (x4[t].z + x4[t].w);
+            }
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const int kk = sb * SB + g * 32 + lane;
-                float xv[QM_T], qv[QM_T];
+            for (int r = 0; r < QM_RW; ++r) {
+                if (row0 + r >= rows) continue;
+                const uint8_t *rb = wb + (warp * QM_RW + r) * CBP;
+                float wq[4], off = 0.f;                           // weight e = wq[e] - off
+                if (KIND == 8) {
+                    const uint8_t *b = rb + (c >> 5) * BB;          // 34-byte block of this group
+                    const float d = ld_half(b);
+                    const uint32_t lo = *reinterpret_cast<const uint16_t *>(b + 2 + lc);
+                    const uint32_t hi = *reinterpret_cast<const uint16_t *>(b + 4 + lc);
+                    const uint32_t q = lo | (hi << 16);
 #pragma unroll
-                for (int t = 0; t < QM_T; ++t) {
-                    xv[t] = xs[t][kk];
-                    qv[t] = FAST ? qs[FAST ? t : 0][FAST ? kk : 0] : 0.f;
+                    for (int e = 0; e < 4; ++e) wq[e] = d * (float)(int8_t)(q >> (8 * e));
+                } else if (KIND == 12) {
+                    // 6-bit scale and minimum of group g from the 12 packed bytes
+                    const int g = c >> 5;                         // group within the 256-column block
+                    const uint8_t *sc = rb + 4;
+                    const int lo6 = g < 4 ? sc[g] : sc[g + 4];
+                    const int hi2s = g < 4 ? 0 : (sc[g - 4] >> 6) << 4;
+                    const int zlo = g < 4 ? sc[g + 4] : (sc[g + 4] >> 4);
+                    const int hi2z = g < 4 ? 0 : (sc[g] >> 6) << 4;
+                    const float s6 = (float)(g < 4 ? (lo6 & 63) : ((lo6 & 15) | hi2s));
+                    const float z6 = (float)(g < 4 ? (zlo & 63) : (zlo | hi2z));
+                    const float ds = ld_half(rb) * s6;
+                    off = ld_half(rb + 2) * z6;
+                    const uint32_t q = *reinterpret_cast<const uint32_t *>(rb + 16 + (g >> 1) * 32 + lc) >> (4 * (g & 1));
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) wq[e] = ds * (float)((q >> (8 * e)) & 15);
+                } else {
+                    const int half = c >> 7, quarter = (c >> 5) & 3;
+                    const uint32_t low = *reinterpret_cast<const uint32_t *>(rb + half * 64 + (quarter & 1) * 32 + lc)
+                                         >> (4 * (quarter >> 1));
+                    const uint32_t high = *reinterpret_cast<const uint32_t *>(rb + 128 + half * 32 + lc) >> (2 * quarter);
+                    const float ds = (float)(int8_t)rb[192 + (c >> 4)] * ld_half(rb + 208);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        wq[e] = (float)((int)(((high >> (8 * e)) & 3) * 16 + ((low >> (8 * e)) & 15)) - 32) * ds;
                 }
 #pragma unroll
-                for (int r = 0; r < QM_RW; ++r) {
-                    if (row0 + r >= rows) continue;
-                    const uint8_t *b = base[r];
-                    float wq, off = 0.f;                          // weight = wq - off
-                    if (KIND == 8) {
-                        wq = ld_half(b) * (float)(int8_t)b[2 + lane];
-                    } else if (KIND == 12) {
-                        float s, z;
-                        q4k_scale_min(b + 4, g, s, z);
-                        const int q = (b[16 + (g >> 1) * 32 + lane] >> (4 * (g & 1))) & 15;
-                        wq = ld_half(b) * s * (float)q;
-                        off = ld_half(b + 2) * z;
-                    } else {
-                        const int half = g >> 2, quarter = g & 3;
-                        const int low = (b[half * 64 + (quarter & 1) * 32 + lane] >> (4 * (quarter >> 1))) & 15;
-                        const int high = (b[128 + half * 32 + lane] >> (2 * quarter)) & 3;
-                        const int sc = (int8_t)b[192 + g * 2 + (lane >> 4)];
-                        wq = (float)(high * 16 + low - 32) * (float)sc * ld_half(b + 208);
-                    }
-#pragma unroll
-                    for (int t = 0; t < QM_T; ++t) {
-                        if (FAST) acc[r][t] = fmaf(wq, qv[t], fmaf(-off, xv[t], acc[r][t]));
-                        else acc[r][t] = fmaf(wq - off, xv[t], acc[r][t]);
-                    }
+                for (int t = 0; t < QM_T; ++t) {
+                    float a = fmaf(-off, xsum[t], acc[r][t]);
+                    a = fmaf(wq[0], q4[t].x, a);
+                    a = fmaf(wq[1], q4[t].y, a);
+                    a = fmaf(wq[2], q4[t].z, a);
+                    acc[r][t] = fmaf(wq[3], q4[t].w, a);
                 }
             }
         }
