@@ -21,9 +21,9 @@ def _case(dim, batch=5):
     return I.delta_wave(dim, batch=batch)
 
 
-@pytest.mark.parametrize('dim', [32, 128])
-def test_oracle_commit_replays_the_accepted_prefix(dim):
-    c = _case(dim)
+@pytest.mark.parametrize('dim,batch', [(32, 5), (128, 5), (32, 8), (128, 1)])
+def test_oracle_commit_replays_the_accepted_prefix(dim, batch):
+    c = _case(dim, batch)
     hk, hv, batch = c['key_heads'], c['value_heads'], c['batch']
     C = (2 * hk + hv) * dim
     trace = oracle.delta_trace(c['history'], c['qkv'], c['alpha'], c['beta'], c['conv'], c['decay'], c['bias'],
@@ -62,11 +62,11 @@ def test_verify_and_commit_reject_bad_arguments(lib):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize('dim', [32, 128])
-def test_verify_records_and_commit_rebuilds(hot, dim):
+@pytest.mark.parametrize('dim,batch', [(32, 5), (128, 5), (128, 1), (128, 8)])
+def test_verify_records_and_commit_rebuilds(hot, dim, batch):
     import torch
     dev = torch.device('cuda')
-    c = _case(dim)
+    c = _case(dim, batch)
     hk, hv, batch = c['key_heads'], c['value_heads'], c['batch']
     C = (2 * hk + hv) * dim
     t = lambda k: torch.from_numpy(np.ascontiguousarray(np.asarray(c[k], np.float32).reshape(-1))).to(dev)  # noqa: E731
@@ -94,7 +94,7 @@ def test_verify_records_and_commit_rebuilds(hot, dim):
     bad = np.abs(got - exp_trace) > 3e-5 * (1 + np.abs(exp_trace))
     assert not bad.any(), f'{bad.sum()} trace mismatches, first at {np.argmax(bad)}'
     # commit each acceptance count from the verify's end state
-    for accepted in (0, 1, 3, batch):
+    for accepted in sorted({0, 1, min(3, batch), batch}):
         st, hi = st_v.clone(), hi_v.clone()
         hot.delta_commit(st, hi, saved_s, saved_h, trace, accepted, batch, hk, hv, dim)
         torch.cuda.synchronize()
