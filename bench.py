@@ -627,6 +627,27 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
         res[f'mm_{name}_17408x5120_t8_us'] = round(ms * 1e3, 2)
         res[f'mm_{name}_hbm_frac'] = round(byt / (ms * 1e-3) / 1e9 / hbm_peak, 4)
         del mats
+    # checkpoint / restore: one attention layer's valid K and V prefix at
+    # context 139,264 plus the 48 DeltaNet states and histories, as one span list
+    P_ = 139264 - 8
+    srcs = [torch.empty(P_ * HKV * HD * 2, dtype=torch.uint8, device='cuda') for _ in range(2)]
+    srcs += [torch.empty(HV * DK * DK * 4 + 3 * C_ * 4, dtype=torch.uint8, device='cuda') for _ in range(48)]
+    dsts = [torch.empty_like(t) for t in srcs]
+    pairs = list(zip(dsts, srcs))
+    for _ in range(3):
+        hot.copy_spans(pairs)
+    e0.record()
+    for _ in range(10):
+        hot.copy_spans(pairs)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 10
+    nbytes = sum(t.numel() for t in srcs)
+    res['checkpoint_spans'] = len(pairs)
+    res['checkpoint_mb'] = round(nbytes / 1e6, 1)
+    res['checkpoint_us'] = round(ms * 1e3, 2)
+    res['checkpoint_hbm_frac'] = round(2 * nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4)
+    del srcs, dsts, pairs
     return res
 
 

@@ -133,6 +133,15 @@ size_t qv_mm_weight_bytes(int kind, int width, int rows);
 int qv_mm(float *out, const void *weights, const float *x, int kind, int batch,
           int width, int rows, int fast, void *stream);
 
+/* Checkpoint / restore of the layer state (the reference's Model::copy_state,
+ * src/runtime.cu:455-485, which issues one cudaMemcpy per attention KV prefix
+ * and per DeltaNet state / history): copies `count` (1..160) spans
+ * dst[i] <- src[i] of bytes[i] bytes in one launch.  dst, src and bytes are
+ * host arrays of device addresses and sizes (read during the call); the
+ * spans must not overlap each other.  Asynchronous on `stream`. */
+int qv_copy_spans(void *const *dst, const void *const *src, const size_t *bytes,
+                  int count, void *stream);
+
 /* Verify transaction of a DeltaNet layer, the state side of the reference's
  * qv_verify / qv_commit (src/runtime.h:57-68; src/runtime.cu:363-374 saves the
  * start state and history and records the transitions, src/runtime.cu:389-395

@@ -52,6 +52,11 @@ size_t projection_weight_bytes(int kind, int width, int rows);
 void projection_run(float *out, const void *weights, const float *x, int kind, int T, int width, int rows,
                     bool fast, cudaStream_t st);
 
+// Checkpoint / restore (copy.cu): copy up to MAX_COPY_SPANS (dst, src, bytes)
+// device spans in one launch.
+constexpr int MAX_COPY_SPANS = 160;
+void copy_spans(void *const *dst, const void *const *src, const size_t *bytes, int count, cudaStream_t st);
+
 // Chunked gated DeltaNet prefill (gdn_chunk.cu): same inputs / outputs as
 // delta_core_recurrent, D = 128, chunks of 64 tokens on tcgen05.
 size_t delta_chunked_workspace_bytes(int T, int Hv);

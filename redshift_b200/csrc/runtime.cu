@@ -336,6 +336,15 @@ int qv_delta(float *out, float *state, float *history, const float *qkv, const f
     });
 }
 
+int qv_copy_spans(void *const *dst, const void *const *src, const size_t *bytes, int count, void *stream) {
+    return guarded([&] {
+        require(count >= 1 && count <= qv::MAX_COPY_SPANS, "span count must be 1..160");
+        require(dst && src && bytes, "null span table");
+        for (int i = 0; i < count; ++i) require(bytes[i] == 0 || (dst[i] && src[i]), "null span address");
+        qv::copy_spans(dst, src, bytes, count, as_stream(stream));
+    });
+}
+
 size_t qv_mm_weight_bytes(int kind, int width, int rows) {
     if (!(kind == 8 || kind == 12 || kind == 14) || width <= 0 || rows <= 0 || width % (kind == 8 ? 32 : 256))
         return 0;

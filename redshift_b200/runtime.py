@@ -46,6 +46,7 @@ ADDITIVE_SIGNATURES = {
     'qv_delta': ([_P] * 11 + [_I] * 4 + [_F, _P], _I),
     'qv_delta_trace_floats': ([_I, _I, _I], _S),
     'qv_mm_weight_bytes': ([_I, _I, _I], _S),
+    'qv_copy_spans': ([_P, _P, _P, _I, _P], _I),
     'qv_mm': ([_P] * 3 + [_I] * 5 + [_P], _I),
     'qv_delta_verify': ([_P] * 11 + [_I] * 4 + [_F] + [_P] * 4, _I),
     'qv_delta_commit': ([_P] * 5 + [_I] * 5 + [_P], _I),
@@ -176,6 +177,15 @@ class HotPath:
         self.check(self.lib.qv_delta(p(out), p(state), p(history), p(qkv), p(gate), p(alpha), p(beta),
                                      p(conv), p(decay), p(bias), p(norm), batch, key_heads, value_heads, dim,
                                      epsilon, self._stream()))
+
+    def copy_spans(self, pairs):
+        """qv_copy_spans over [(dst_tensor, src_tensor[, bytes]), ...] (whole tensors by default)."""
+        import ctypes
+        n = len(pairs)
+        dst = (ctypes.c_void_p * n)(*[d.data_ptr() for d, s, *_ in pairs])
+        src = (ctypes.c_void_p * n)(*[s.data_ptr() for d, s, *_ in pairs])
+        nb = (ctypes.c_size_t * n)(*[(rest[0] if rest else s.numel() * s.element_size()) for d, s, *rest in pairs])
+        self.check(self.lib.qv_copy_spans(dst, src, nb, n, self._stream()))
 
     def mm(self, out, weights, x, kind, batch, width, rows, fast=False):
         """qv_mm: out [batch][rows] = W x for a block-quantized W on the device."""
