@@ -47,9 +47,13 @@ __host__ __device__ constexpr size_t delta_trace_floats(int C, int Hv) { return 
 //
 // Grid: CPH CTAs per value head (a cluster); every CTA must own an SM, since
 // an SM holding two CTAs would double the time of its whole cluster.
-// Thread layout: 8 threads per state row, D/8 columns each (columns
-// 32i + 4j + e), so a row's dot products reduce with 3 shuffles; every thread
-// also filters one conv channel.  Per chunk of <= 8 tokens:
+// Thread layout: every thread filters one conv channel; the token loop runs
+// on the first 4 * rows threads, 8 per PAIR of state rows and D/8 columns of
+// each (columns 32i + 4j + e), so every k/q value read from shared memory
+// serves two rows (the loop is bound by shared-memory bandwidth) and the four
+// dot products of a token (S_a.k, S_b.k, S_a.q, S_b.q, all against the state
+// before the token's update) reduce together in 4 shuffles.  Per chunk of
+// <= 8 tokens:
 //  * the chunk's inputs are loaded one chunk ahead (chunk 0 with the
 //    prologue), so their latency overlaps the previous chunk's scan;
 //  * each CTA filters (conv + SiLU) all q/k channels of its key head and its
@@ -81,13 +85,16 @@ delta_kernel(const DeltaArgs a) {
     const int Hk = a.Hk, Hv = a.Hv, kh = h % Hk;
     const int C = (2 * Hk + Hv) * D;
     const int row0 = rank * D / CPH, rows = (rank + 1) * D / CPH - row0;   // this CTA's head rows
-    const int r = tid >> 3, j = tid & 7;          // local row, column group
-    const bool has_row = r < rows;
+    // token loop: the first 4 * rows threads, 8 per PAIR of state rows (rows
+    // ra, rb), D/8 columns of each; every k/q value read from shared memory
+    // serves both rows
+    const int j = tid & 7, ra = 2 * (tid >> 3), rb = ra + 1;
+    const bool has_a = ra < rows, has_b = rb < rows, scans = tid < 4 * MAXR;
 
     __shared__ __align__(16) float Fq[CHUNK][D], Fk[CHUNK][D], Fv[CHUNK][MAXR];
     __shared__ __align__(16) float O[CHUNK][MAXR];
     __shared__ float wsum[NW][CHUNK];             // per-warp sums of q^2 or k^2
-    __shared__ float scal[CHUNK][4];              // sq, sk, decay, beta
+    __shared__ __align__(16) float scal[CHUNK][8];  // sq, sk, decay, beta, k.q
     __shared__ float osum[2][CPH][CHUNK];         // sums of o^2 pushed by each rank, by chunk parity
     __shared__ __align__(8) uint64_t osum_bar[2];
     __shared__ bool norm_ok;
@@ -106,15 +113,20 @@ delta_kernel(const DeltaArgs a) {
     if (tid == 0) launch_dependents();
 
     // ---- loads that do not depend on the chunk
-    float S[COLS];
-    float *srow = a.state + ((size_t)h * D + row0 + (has_row ? r : 0)) * D;
+    float Sa[COLS], Sb[COLS];
+    float *srow_a = a.state + ((size_t)h * D + row0 + (has_a ? ra : 0)) * D;
+    float *srow_b = a.state + ((size_t)h * D + row0 + (has_b ? rb : 0)) * D;
 #pragma unroll
     for (int i = 0; i < NV4; ++i) {
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (has_row) v = *reinterpret_cast<const float4 *>(srow + 32 * i + 4 * j);
-        S[4 * i] = v.x; S[4 * i + 1] = v.y; S[4 * i + 2] = v.z; S[4 * i + 3] = v.w;
-        if (RECORD && has_row)
-            *reinterpret_cast<float4 *>(a.saved_state + (srow - a.state) + 32 * i + 4 * j) = v;
+        float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+        if (has_a) va = *reinterpret_cast<const float4 *>(srow_a + 32 * i + 4 * j);
+        if (has_b) vb = *reinterpret_cast<const float4 *>(srow_b + 32 * i + 4 * j);
+        Sa[4 * i] = va.x; Sa[4 * i + 1] = va.y; Sa[4 * i + 2] = va.z; Sa[4 * i + 3] = va.w;
+        Sb[4 * i] = vb.x; Sb[4 * i + 1] = vb.y; Sb[4 * i + 2] = vb.z; Sb[4 * i + 3] = vb.w;
+        if (RECORD && has_a)
+            *reinterpret_cast<float4 *>(a.saved_state + (srow_a - a.state) + 32 * i + 4 * j) = va;
+        if (RECORD && has_b)
+            *reinterpret_cast<float4 *>(a.saved_state + (srow_b - a.state) + 32 * i + 4 * j) = vb;
     }
     // Conv channel of this thread: e < D -> q, e < 2D -> k, e < 2D + rows -> v row.
     const int e = tid;
@@ -208,6 +220,14 @@ delta_kernel(const DeltaArgs a) {
             scal[tid][2] = expf(decay_h * softplusf_(al + bias_h));
             scal[tid][3] = sigmoidf_(be);
         }
+        // k.q of each token (filtered, not normalised), one warp per token
+        for (int tt = warp; tt < n; tt += NW) {
+            float x = 0.f;
+#pragma unroll
+            for (int i = 0; i < D / 32; ++i) x = fmaf(Fq[tt][lane + 32 * i], Fk[tt][lane + 32 * i], x);
+            x = warp_sum(x);
+            if (lane == 0) scal[tt][4] = x;
+        }
         __syncthreads();
         if (RECORD) {
             // transition trace (recorded calls have a single chunk)
@@ -228,41 +248,62 @@ delta_kernel(const DeltaArgs a) {
         }
         // ---- delta rule over the chunk: S = a S; u = S k; delta = beta (v - u);
         //      S += delta k^T; o = S q   (k, q normalised through sk, sq).  The
-        //      decay is applied inside the update: u = a (S k), S = a S + delta k.
+        //      decay is applied inside the update: u = a (S k), S = a S + delta k,
+        //      and the readout is o = a (S q) + delta (k.q): both dot products are
+        //      taken against the state before the token's update and reduced
+        //      together across the pair's 8 lanes by a transposing butterfly
+        //      (lanes j = 0,1: S_a.k, 2,3: S_b.k, 4,5: S_a.q, 6,7: S_b.q).
+        if (scans) {
 #pragma unroll
-        for (int tt = 0; tt < CHUNK; ++tt) {
-            if (tt >= n) break;
-            const float sqn = scal[tt][0], skn = scal[tt][1], decay = scal[tt][2], beta = scal[tt][3];
-            const float *kk = Fk[tt], *qq = Fq[tt];
-            float4 k4[NV4];
-            float u0 = 0.f, u1 = 0.f;
+            for (int tt = 0; tt < CHUNK; ++tt) {
+                if (tt >= n) break;
+                const float4 sc = *reinterpret_cast<const float4 *>(scal[tt]);
+                const float sqn = sc.x, skn = sc.y, decay = sc.z, beta = sc.w, kq = scal[tt][4];
+                const float4 *kk = reinterpret_cast<const float4 *>(Fk[tt]);
+                const float4 *qq = reinterpret_cast<const float4 *>(Fq[tt]);
+                float4 k4[NV4];
+                float ua0 = 0.f, ua1 = 0.f, ub0 = 0.f, ub1 = 0.f, wa0 = 0.f, wa1 = 0.f, wb0 = 0.f, wb1 = 0.f;
 #pragma unroll
-            for (int i = 0; i < NV4; ++i) {
-                k4[i] = *reinterpret_cast<const float4 *>(kk + 32 * i + 4 * j);
-                u0 += S[4 * i] * k4[i].x; u1 += S[4 * i + 1] * k4[i].y;
-                u0 += S[4 * i + 2] * k4[i].z; u1 += S[4 * i + 3] * k4[i].w;
+                for (int i = 0; i < NV4; ++i) {
+                    k4[i] = kk[8 * i + j];
+                    const float4 q4 = qq[8 * i + j];
+                    ua0 = fmaf(Sa[4 * i], k4[i].x, ua0); ua1 = fmaf(Sa[4 * i + 1], k4[i].y, ua1);
+                    ua0 = fmaf(Sa[4 * i + 2], k4[i].z, ua0); ua1 = fmaf(Sa[4 * i + 3], k4[i].w, ua1);
+                    ub0 = fmaf(Sb[4 * i], k4[i].x, ub0); ub1 = fmaf(Sb[4 * i + 1], k4[i].y, ub1);
+                    ub0 = fmaf(Sb[4 * i + 2], k4[i].z, ub0); ub1 = fmaf(Sb[4 * i + 3], k4[i].w, ub1);
+                    wa0 = fmaf(Sa[4 * i], q4.x, wa0); wa1 = fmaf(Sa[4 * i + 1], q4.y, wa1);
+                    wa0 = fmaf(Sa[4 * i + 2], q4.z, wa0); wa1 = fmaf(Sa[4 * i + 3], q4.w, wa1);
+                    wb0 = fmaf(Sb[4 * i], q4.x, wb0); wb1 = fmaf(Sb[4 * i + 1], q4.y, wb1);
+                    wb0 = fmaf(Sb[4 * i + 2], q4.z, wb0); wb1 = fmaf(Sb[4 * i + 3], q4.w, wb1);
+                }
+                const float ua = ua0 + ua1, ub = ub0 + ub1, wa = wa0 + wa1, wb = wb0 + wb1;
+                const bool hi4 = (j & 4) != 0, hi2 = (j & 2) != 0;
+                float m0 = hi4 ? wa : ua, m1 = hi4 ? wb : ub;
+                m0 += __shfl_xor_sync(0xffffffffu, hi4 ? ua : wa, 4);
+                m1 += __shfl_xor_sync(0xffffffffu, hi4 ? ub : wb, 4);
+                float m = hi2 ? m1 : m0;
+                m += __shfl_xor_sync(0xffffffffu, hi2 ? m0 : m1, 2);
+                m += __shfl_xor_sync(0xffffffffu, m, 1);
+                // delta of row a on lanes 0-1, of row b on lanes 2-3; broadcast to the pair
+                const int rl = hi2 ? rb : ra;
+                const float vrow = rl < rows ? Fv[tt][rl] : 0.f;
+                const float dl = (vrow - decay * m * skn) * beta * skn;
+                const int base = lane & ~7;
+                const float da = __shfl_sync(0xffffffffu, dl, base), db = __shfl_sync(0xffffffffu, dl, base + 2);
+                // readout of row a on lane 4, of row b on lane 6
+                if ((j == 4 || j == 6) && rl < rows) O[tt][rl] = sqn * fmaf(decay, m, (hi2 ? db : da) * kq);
+#pragma unroll
+                for (int i = 0; i < NV4; ++i) {
+                    Sa[4 * i] = fmaf(Sa[4 * i], decay, k4[i].x * da);
+                    Sa[4 * i + 1] = fmaf(Sa[4 * i + 1], decay, k4[i].y * da);
+                    Sa[4 * i + 2] = fmaf(Sa[4 * i + 2], decay, k4[i].z * da);
+                    Sa[4 * i + 3] = fmaf(Sa[4 * i + 3], decay, k4[i].w * da);
+                    Sb[4 * i] = fmaf(Sb[4 * i], decay, k4[i].x * db);
+                    Sb[4 * i + 1] = fmaf(Sb[4 * i + 1], decay, k4[i].y * db);
+                    Sb[4 * i + 2] = fmaf(Sb[4 * i + 2], decay, k4[i].z * db);
+                    Sb[4 * i + 3] = fmaf(Sb[4 * i + 3], decay, k4[i].w * db);
+                }
             }
-            float u = u0 + u1;
-            u += __shfl_xor_sync(0xffffffffu, u, 1);
-            u += __shfl_xor_sync(0xffffffffu, u, 2);
-            u += __shfl_xor_sync(0xffffffffu, u, 4);
-            const float delta = ((has_row ? Fv[tt][r] : 0.f) - decay * u * skn) * beta * skn;
-            float o0 = 0.f, o1 = 0.f;
-#pragma unroll
-            for (int i = 0; i < NV4; ++i) {
-                const float4 q4 = *reinterpret_cast<const float4 *>(qq + 32 * i + 4 * j);
-                S[4 * i] = fmaf(S[4 * i], decay, k4[i].x * delta);
-                S[4 * i + 1] = fmaf(S[4 * i + 1], decay, k4[i].y * delta);
-                S[4 * i + 2] = fmaf(S[4 * i + 2], decay, k4[i].z * delta);
-                S[4 * i + 3] = fmaf(S[4 * i + 3], decay, k4[i].w * delta);
-                o0 += S[4 * i] * q4.x; o1 += S[4 * i + 1] * q4.y;
-                o0 += S[4 * i + 2] * q4.z; o1 += S[4 * i + 3] * q4.w;
-            }
-            float o = o0 + o1;
-            o += __shfl_xor_sync(0xffffffffu, o, 1);
-            o += __shfl_xor_sync(0xffffffffu, o, 2);
-            o += __shfl_xor_sync(0xffffffffu, o, 4);
-            if (j == 0 && has_row) O[tt][r] = o * sqn;
         }
         __syncthreads();
         if (CORE) {
@@ -296,11 +337,14 @@ delta_kernel(const DeltaArgs a) {
         __syncthreads();
     }
 
-    if (has_row) {
 #pragma unroll
-        for (int i = 0; i < NV4; ++i)
-            *reinterpret_cast<float4 *>(srow + 32 * i + 4 * j) =
-                make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+    for (int i = 0; i < NV4; ++i) {
+        if (has_a)
+            *reinterpret_cast<float4 *>(srow_a + 32 * i + 4 * j) =
+                make_float4(Sa[4 * i], Sa[4 * i + 1], Sa[4 * i + 2], Sa[4 * i + 3]);
+        if (has_b)
+            *reinterpret_cast<float4 *>(srow_b + 32 * i + 4 * j) =
+                make_float4(Sb[4 * i], Sb[4 * i + 1], Sb[4 * i + 2], Sb[4 * i + 3]);
     }
     // History: v channels belong to their rows' CTA; the q/k channels of key
     // head kh are written by rank 0 of value head kh (h < Hk) only.
