@@ -187,14 +187,14 @@ class Step:
         from redshift_b200.sharding import PeerExchange, plan
         self.exchange = PeerExchange(self.hot, dist, plan(self.position, self.world, self.rank, self.T))
 
-    def attention_layer(self, a, slot=0):
+    def attention_layer(self, a, seq=0):
         hot, T = self.hot, self.T
         if self.world == 1:
             hot.attention(a['out'], a['kc'], a['vc'], a['q_gate'], a['key'], a['value'], self.ones, self.ones,
                           T, self.position, workspace=self.ws)
         elif self.exchange is not None:
             self.exchange(a['out'], a['kc'], a['vc'], a['q_gate'], a['key'], a['value'], self.ones, self.ones,
-                          T, self.position, slot, workspace=self.ws)
+                          T, self.position, seq, workspace=self.ws)
         else:
             import torch.distributed as dist
             hot.attention_shard(self.part, self.lse, a['kc'], a['vc'], self.begin, self.rows, a['q_gate'],
@@ -213,7 +213,7 @@ class Step:
             if layer % 4 == 3:
                 if events is not None:
                     events[ai][0].record()
-                self.attention_layer(self.attn[ai], slot=ai & 1)
+                self.attention_layer(self.attn[ai], seq=ai)
                 if events is not None:
                     events[ai][1].record()
                 ai += 1
@@ -265,7 +265,7 @@ class Step:
         for layer in range(LAYERS):
             main.wait_event(ready[layer])
             if layer % 4 == 3:
-                self.attention_layer(self.attn[ai], slot=ai & 1)
+                self.attention_layer(self.attn[ai], seq=ai)
                 dev, host = self.h_out_attn[ai]
                 ai += 1
             else:
@@ -557,7 +557,7 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
     torch.cuda.synchronize()
     res['delta_prefill_4096_recurrent_us'] = round(e0.elapsed_time(e1) * 1e3, 2)
     del ws, qd, kd, vd, od
-    # verify/commit transaction (SURVEY 8(f) f1): 48 DeltaNet layers with distinct states,
+    # verify/commit transaction: 48 DeltaNet layers with distinct states,
     # plain layer vs recorded verify, and the commit of 3 of 8 tokens, each replayed as a graph
     T8, C_ = 8, (2 * HK + HV) * DK
     f32 = dict(device='cuda', dtype=torch.float32)
@@ -598,7 +598,7 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
         graph.reset()
         del graph
     del layers
-    # quantized projections (SURVEY 8(f) f3): verify batch of 8 through a 17408 x 5120
+    # quantized projections: verify batch of 8 through a 17408 x 5120
     # matrix (the model's FFN shape), four distinct matrices in rotation (> L2)
     for kind, name in ((8, 'q8_0'), (12, 'q4_k'), (14, 'q6_k')):
         wbytes = int(hot.lib.qv_mm_weight_bytes(kind, 5120, 17408))
@@ -627,7 +627,7 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
         res[f'mm_{name}_17408x5120_t8_us'] = round(ms * 1e3, 2)
         res[f'mm_{name}_hbm_frac'] = round(byt / (ms * 1e-3) / 1e9 / hbm_peak, 4)
         del mats
-    # checkpoint / restore (SURVEY 8(f) f4): one attention layer's valid K and V prefix at
+    # checkpoint / restore: one attention layer's valid K and V prefix at
     # context 139,264 plus the 48 DeltaNet states and histories, as one span list
     P_ = 139264 - 8
     srcs = [torch.empty(P_ * HKV * HD * 2, dtype=torch.uint8, device='cuda') for _ in range(2)]

@@ -204,16 +204,22 @@ int qv_attention_merge(float *out, const float *partials, const float *lses, int
  * call and mapped into this process (CUDA IPC / symmetric memory).  Each
  * rank stores its partial into every buffer and raises a flag there, then
  * waits (bounded; on timeout qv_status reports it) for all ranks' flags.
- * `slot` (0/1) must alternate between consecutive calls on the same buffers.
- * All ranks must make the same sequence of calls.  world 1..8, batch 1..10;
- * out [batch,24,256] is the gated output, identical on every rank. */
+ * `sequence` (>= 0) numbers the calls on the same buffers: the same value on
+ * every rank, one more for each call (n, n+1, n+2, ...; after the first call
+ * it may restart at any value of the other parity).  Its parity selects one
+ * of two buffer slots and its low 24 bits tag every exchanged word, so a word
+ * that arrives after its reader timed out is never accepted by a later call;
+ * a call that reported a timeout has an undefined `out`, the buffers stay
+ * usable.  All ranks must make the same sequence of calls.  world 1..8,
+ * batch 1..10; out [batch,24,256] is the gated output, identical on every
+ * rank. */
 size_t qv_attention_exchange_bytes(int world);
 int qv_attention_shard_exchange(float *out, void *key_cache, void *value_cache,
                                 int shard_begin, int shard_rows,
                                 const float *q_gate, const float *key, const float *value,
                                 const float *q_norm, const float *k_norm,
                                 int batch, int position, float epsilon,
-                                const void *peer_buffers, int world, int rank, int slot,
+                                const void *peer_buffers, int world, int rank, int sequence,
                                 void *workspace, size_t workspace_bytes, void *stream);
 
 /* Core causal prefill attention (no norm, RoPE or gate), device memory:

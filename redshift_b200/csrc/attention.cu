@@ -790,28 +790,35 @@ attn_combine_kernel(float *out, float *out_lse, const float *part_o, const float
 // reads the other ranks' partials of the row from its own buffer and merges
 // them (O = sum_g exp(lse_g - LSE) O_g, times sigmoid(gate)).
 //
-// Every value travels as a 64-bit word {value bits, EX_FLAG}: the reader
-// spins on each of its words until the flag appears, so no fence or separate
-// flag write is needed, and it zeroes each word after reading it.  Receive
-// buffer of each rank: [2 slots][world][EX_ROWS][EX_WORDS] words (256 O, lse,
-// padding).  `slot` alternates between consecutive calls: a rank writes into
-// a slot again two calls later, after it has received this rank's partials of
-// the call in between, and that call started only after this one (and its
-// zeroing) completed.  The CTAs of one launch hold no shared memory to speak
-// of, so all of them are resident at once and every awaited word has a
-// running writer on its rank.
+// Every value travels as a 64-bit word {value bits, tag}: the reader spins on
+// each of its words until the tag of this call appears, so no fence or
+// separate flag write is needed, and it zeroes each word after reading it.
+// Receive buffer of each rank: [2 slots][world][EX_ROWS][EX_WORDS] words (256
+// O, lse, padding).  `seq` counts the calls on these buffers (the same on
+// every rank, +1 per call): its parity picks the slot and its low 24 bits are
+// in the tag.  A rank writes into a slot again two calls later, after it has
+// received this rank's partials of the call in between, and that call started
+// only after this one (and its zeroing) completed.  A word that arrives after
+// its reader gave up (a timeout) stays behind unread, but it carries the tag
+// of its own call and the next call on that slot waits for a different tag,
+// so it is never taken for new data.  The CTAs of one launch hold no shared
+// memory to speak of, so all of them are resident at once and every awaited
+// word has a running writer on its rank.
 constexpr int EX_ROWS = MAX_DECODE_T * NQ;       // rows of the largest decode batch
 constexpr int EX_WORDS = 264;                    // words per row: 256 O + lse, padded to 64 bytes
 constexpr int EX_MAX_WORLD = 8;
-constexpr uint32_t EX_FLAG = 0x5156u;            // high half of a filled word
+__host__ __device__ constexpr uint32_t ex_tag(int seq) {   // high half of a filled word; never 0
+    return 0x51000000u | ((uint32_t)seq & 0x00FFFFFFu);
+}
 __host__ __device__ constexpr size_t ex_bytes(int world) {
     return (size_t)2 * world * EX_ROWS * EX_WORDS * sizeof(uint64_t);
 }
 
 __global__ void __launch_bounds__(256)
 attn_exchange_kernel(float *out, const float *part_o, const float *part_ml, int splits, const float *q_gate,
-                     const uint64_t *peers, int world, int rank, int slot) {
-    const int d = threadIdx.x, row = blockIdx.x;
+                     const uint64_t *peers, int world, int rank, int seq) {
+    const int d = threadIdx.x, row = blockIdx.x, slot = seq & 1;
+    const uint32_t tag32 = ex_tag(seq);
     const int t = row / NQ, h = row % NQ, g = h / GROUP, r = t * GROUP + h % GROUP;
     __shared__ float wgt[MAX_SPLITS], red[2], den_s, lse_s[EX_MAX_WORLD];
     grid_dependency_wait();
@@ -851,7 +858,7 @@ attn_exchange_kernel(float *out, const float *part_o, const float *part_ml, int 
     const float lse = den > 0.f ? (M + log2f(den)) * 0.6931471805599453f : -INFINITY;
 
     // ---- push it to every other rank
-    const uint64_t tag = (uint64_t)EX_FLAG << 32;
+    const uint64_t tag = (uint64_t)tag32 << 32;
     for (int q = 0; q < world; ++q) {
         if (q == rank) continue;
         uint64_t *dst = reinterpret_cast<uint64_t *>(peers[q]) +
@@ -867,7 +874,7 @@ attn_exchange_kernel(float *out, const float *part_o, const float *part_ml, int 
     const long long t0 = clock64();
     bool ok = true;
     auto finish = [&](uint64_t *word, uint64_t x, float fallback) {
-        while ((uint32_t)(x >> 32) != EX_FLAG) {
+        while ((uint32_t)(x >> 32) != tag32) {
             if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok = false; return fallback; }
             x = ld_word_sys(word);
         }
@@ -975,15 +982,17 @@ void check_launch(const char *what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-bool configured = false;
+// The shared-memory limit of a kernel is a per-device attribute: set it on
+// every device the process launches on.
+PerDeviceOnce g_configured;
 void configure() {
-    if (configured) return;
-    if (cudaFuncSetAttribute(fa_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             FaLayout<true>::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(fa_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             FaLayout<false>::SMEM_BYTES) != cudaSuccess)
-        throw std::runtime_error("cannot reserve shared memory for the attention kernel");
-    configured = true;
+    g_configured.run([] {
+        if (cudaFuncSetAttribute(fa_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 FaLayout<true>::SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(fa_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 FaLayout<false>::SMEM_BYTES) != cudaSuccess)
+            throw std::runtime_error("cannot reserve shared memory for the attention kernel");
+    });
 }
 
 struct Split { int tiles, splits; };
@@ -1090,16 +1099,16 @@ int attention_exchange_max_world() { return EX_MAX_WORLD; }
 void attention_shard_exchange(float *out, __half *kc, __half *vc, const float *q_gate, const float *key,
                               const float *value, const float *qn, const float *kn, int T, int position,
                               int kv_begin, int kv_rows, bool append, float eps, const uint64_t *peers,
-                              int world, int rank, int slot, void *ws, size_t ws_bytes, cudaStream_t st) {
+                              int world, int rank, int seq, void *ws, size_t ws_bytes, cudaStream_t st) {
     if (!decode_regime(T)) throw std::invalid_argument("the exchange supports decode batches only");
-    if (world < 1 || world > EX_MAX_WORLD || rank < 0 || rank >= world || (slot != 0 && slot != 1))
+    if (world < 1 || world > EX_MAX_WORLD || rank < 0 || rank >= world || seq < 0)
         throw std::invalid_argument("invalid exchange group");
     if (ws_bytes < attention_workspace_bytes(T, kv_rows)) throw std::invalid_argument("attention workspace too small");
     const DecodeParts parts = decode_parts(ws, decode_split(kv_rows));
     const Split sp = launch_decode(kc, vc, q_gate, key, value, qn, kn, T, position, kv_begin, kv_rows, append, eps,
                                    parts, st);
     const cudaError_t e = launch_chained(attn_exchange_kernel, dim3(T * NQ), dim3(256), 0, st, out, parts.o, parts.ml,
-                                         sp.splits, q_gate, peers, world, rank, slot);
+                                         sp.splits, q_gate, peers, world, rank, seq);
     if (e != cudaSuccess) throw std::runtime_error(std::string("attention exchange: ") + cudaGetErrorString(e));
 }
 

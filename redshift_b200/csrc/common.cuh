@@ -10,6 +10,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+#include <stdexcept>
 #include <utility>
 
 namespace qv {
@@ -281,6 +284,30 @@ __device__ __forceinline__ float exp2_approx(float x) {
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x * sigmoidf_(x); }
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+// ---------------------------------------------------------------- host set-up
+// Runs a set-up step once per CUDA device, with that device current.  Kernel
+// attributes such as the dynamic shared-memory limit are kept per device by
+// the runtime, so a process that drives several GPUs must set them on each;
+// concurrent first calls from several host threads run the step once.
+class PerDeviceOnce {
+  public:
+    template <class F> void run(F &&setup) {
+        int dev = -1;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+            throw std::runtime_error("no usable current CUDA device");
+        if (done_[dev].load(std::memory_order_acquire)) return;
+        std::lock_guard<std::mutex> guard(lock_);
+        if (done_[dev].load(std::memory_order_relaxed)) return;
+        setup();
+        done_[dev].store(true, std::memory_order_release);
+    }
+
+  private:
+    static constexpr int kMaxDevices = 64;
+    std::mutex lock_;
+    std::atomic<bool> done_[kMaxDevices] = {};
+};
 
 // ---------------------------------------------------------------- host launch
 // Launch `kernel` on `stream` with programmatic stream serialisation: its CTAs

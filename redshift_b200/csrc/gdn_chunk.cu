@@ -694,7 +694,8 @@ GdnWorkspace carve(void *ws, int Hv, int nch) {
     return g;
 }
 
-bool gdn_configured = false;
+// The shared-memory limit of a kernel is a per-device attribute.
+PerDeviceOnce g_gdn_configured;
 }  // namespace
 
 size_t delta_chunked_workspace_bytes(int T, int Hv) {
@@ -708,12 +709,11 @@ void delta_chunked(float *out, float *state, const __half *q, const __half *k, c
     if (D != GD) throw std::invalid_argument("the chunked DeltaNet path needs head dimension 128");
     if (T < 1 || Hk < 1 || Hv < 1) throw std::invalid_argument("invalid DeltaNet dimensions");
     if (ws_bytes < delta_chunked_workspace_bytes(T, Hv)) throw std::invalid_argument("DeltaNet workspace too small");
-    if (!gdn_configured) {
+    g_gdn_configured.run([] {
         if (cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM) != cudaSuccess ||
             cudaFuncSetAttribute(gdn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM) != cudaSuccess)
             throw std::runtime_error("cannot reserve shared memory for the chunked DeltaNet kernels");
-        gdn_configured = true;
-    }
+    });
     const int nch = (T + GC - 1) / GC;
     const GdnWorkspace w = carve(ws, Hv, nch);
     GdnPrep pp{q, k, alpha, beta, decay, bias, w.th, w.tl, w.tp, w.mq, w.sc, T, Hk, Hv, nch};

@@ -23,7 +23,7 @@ int attention_exchange_max_world();
 void attention_shard_exchange(float *out, __half *kc, __half *vc, const float *q_gate, const float *key,
                               const float *value, const float *qn, const float *kn, int T, int position,
                               int kv_begin, int kv_rows, bool append, float eps, const uint64_t *peers,
-                              int world, int rank, int slot, void *ws, size_t ws_bytes, cudaStream_t st);
+                              int world, int rank, int seq, void *ws, size_t ws_bytes, cudaStream_t st);
 void prefill_core(float *out, float *lse, const __half *q, const __half *kc, const __half *vc, int T,
                   int position, cudaStream_t st);
 

@@ -6,9 +6,9 @@
 // treats any later allocation as a failure, or a plugin host that owns every
 // allocation and gives its plugins only the tensors of the call.  This entry
 // point needs nothing from them but the inputs and outputs: its scratch space
-// (the prepared queries and the split-KV partials) lives in a fixed array in
-// device memory that every GPU holds from the moment the library is loaded
-// until the process exits.
+// (the split-KV partials: each split's unnormalised output rows and their
+// running max and sum) lives in a fixed array in device memory that every GPU
+// holds from the moment the library is loaded until the process exits.
 #include "../../include/runtime.h"
 #include "hotpath.h"
 

@@ -447,7 +447,7 @@ size_t qv_attention_exchange_bytes(int world) {
 int qv_attention_shard_exchange(float *out, void *key_cache, void *value_cache, int shard_begin, int shard_rows,
                                 const float *q_gate, const float *key, const float *value, const float *q_norm,
                                 const float *k_norm, int batch, int position, float epsilon,
-                                const void *peer_buffers, int world, int rank, int slot, void *workspace,
+                                const void *peer_buffers, int world, int rank, int sequence, void *workspace,
                                 size_t workspace_bytes, void *stream) {
     return guarded([&] {
         require(batch >= 1 && batch <= qv::attention_max_shard_batch(), "shard batch must be between 1 and 10");
@@ -458,14 +458,14 @@ int qv_attention_shard_exchange(float *out, void *key_cache, void *value_cache, 
         require(append || shard_begin + shard_rows < position, "shard extends past the verify position");
         require(world >= 1 && world <= qv::attention_exchange_max_world() && rank >= 0 && rank < world,
                 "invalid exchange group");
-        require(slot == 0 || slot == 1, "slot must be 0 or 1");
+        require(sequence >= 0, "the exchange sequence number must not be negative");
         require(out && key_cache && value_cache && q_gate && key && value && q_norm && k_norm && peer_buffers &&
                 workspace, "null attention buffer");
         const int rows = shard_rows + (append ? batch : 0);
         require(rows > 0, "empty shard");
         qv::attention_shard_exchange(out, static_cast<__half *>(key_cache), static_cast<__half *>(value_cache),
                                      q_gate, key, value, q_norm, k_norm, batch, position, shard_begin, rows, append,
-                                     epsilon, static_cast<const uint64_t *>(peer_buffers), world, rank, slot,
+                                     epsilon, static_cast<const uint64_t *>(peer_buffers), world, rank, sequence,
                                      workspace, workspace_bytes, as_stream(stream));
     });
 }

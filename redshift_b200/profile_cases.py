@@ -53,12 +53,12 @@ def make_case(hot, case, size):
         ws = torch.empty(hot.lib.qv_attention_shard_workspace(T, ctx - T), dtype=torch.uint8, device=dev)
         buf = torch.zeros(hot.lib.qv_attention_exchange_bytes(1) // 4, dtype=torch.float32, device=dev)
         peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
-        state = {'slot': 0}
+        state = {'seq': 0}
 
         def run():
             hot.attention_shard_exchange(out, kc, vc, 0, ctx - T, qg, key, val, ones, ones, T, ctx - T, peers, 1, 0,
-                                         state['slot'], workspace=ws)
-            state['slot'] ^= 1
+                                         state['seq'], workspace=ws)
+            state['seq'] += 1
         run.keep = (buf, peers)
         return run
     if case in ('delta', 'delta_core', 'delta_chunked'):

@@ -149,15 +149,16 @@ class HotPath:
                                                self._stream()))
 
     def attention_shard_exchange(self, out, key_cache, value_cache, shard_begin, shard_rows, q_gate, key, value,
-                                 q_norm, k_norm, batch, position, peers, world, rank, slot, epsilon=1e-6,
+                                 q_norm, k_norm, batch, position, peers, world, rank, sequence, epsilon=1e-6,
                                  workspace=None):
-        """Shard attention + peer-memory exchange + merge (``peers``: int64 device tensor of buffer addresses)."""
+        """Shard attention + peer-memory exchange + merge (``peers``: int64 device tensor of buffer
+        addresses; ``sequence``: the call's number on these buffers, +1 per call, the same on every rank)."""
         need = self.lib.qv_attention_shard_workspace(batch, shard_rows)
         ws = workspace if workspace is not None else self.workspace(need, out.device)
         p = self._ptr
         self.check(self.lib.qv_attention_shard_exchange(
             p(out), p(key_cache), p(value_cache), shard_begin, shard_rows, p(q_gate), p(key), p(value), p(q_norm),
-            p(k_norm), batch, position, epsilon, p(peers), world, rank, slot, p(ws), ws.numel() * ws.element_size(),
+            p(k_norm), batch, position, epsilon, p(peers), world, rank, sequence, p(ws), ws.numel() * ws.element_size(),
             self._stream()))
 
     def attention_merge(self, out, partials, lses, shards, batch, q_gate):

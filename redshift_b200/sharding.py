@@ -80,10 +80,11 @@ class PeerExchange:
     Allocates each rank's exchange buffer in torch symmetric memory (mapped
     into every rank of ``group``), zeroes it and publishes the rank-ordered
     array of buffer addresses.  Each call runs the shard's attention, stores
-    its (partial, LSE) into every rank's buffer, raises a flag there, waits for
-    the other ranks' flags and merges; no collective library is on the path.
-    ``slot`` must alternate between consecutive calls (e.g. the attention
-    layer's index parity), the same on every rank.
+    its (partial, LSE) into every rank's buffer, tagged with the call's
+    sequence number, waits for the other ranks' words of this call and merges;
+    no collective library is on the path.  ``sequence`` numbers the calls on
+    these buffers, +1 per call and the same on every rank (e.g. the attention
+    layer's index within a step whose layer count is even).
     """
 
     def __init__(self, hot, dist, shard, group=None):
@@ -100,9 +101,9 @@ class PeerExchange:
         torch.cuda.synchronize()
         dist.barrier(group=group)
 
-    def __call__(self, out, key_cache, value_cache, q_gate, key, value, q_norm, k_norm, batch, position, slot,
+    def __call__(self, out, key_cache, value_cache, q_gate, key, value, q_norm, k_norm, batch, position, sequence,
                  epsilon=1e-6, workspace=None):
         s = self.shard
         self.hot.attention_shard_exchange(out, key_cache, value_cache, s.begin, s.rows, q_gate, key, value, q_norm,
-                                          k_norm, batch, position, self.peers, s.world, s.rank, slot, epsilon,
+                                          k_norm, batch, position, self.peers, s.world, s.rank, sequence, epsilon,
                                           workspace=workspace)

@@ -145,3 +145,18 @@ def test_ctypes_signatures_match_the_header():
     for name, argtypes in tables.items():
         assert name in counts, name
         assert len(argtypes) == counts[name], (name, len(argtypes), counts[name])
+
+
+def test_no_alloc_scratch_covers_every_accepted_call(lib):
+    """qv_attention_noalloc's fixed scratch (10 MiB per GPU, the size include/runtime.h states)
+    must hold the workspace of every call it accepts: batch 1..8 at every context up to 139,264.
+    A change to the split-KV plan that outgrows the array fails here, not in a serving call."""
+    scratch = 10 << 20
+    for batch in range(1, 9):
+        positions = sorted(set(range(0, 139264 - batch + 1, 997)) | {139264 - batch})
+        need = max(lib.qv_attention_workspace(batch, p) for p in positions)
+        assert 0 < need <= scratch, (batch, need)
+    v = ct.c_void_p(8)   # never dereferenced: the exchange sequence number is validated first
+    assert lib.qv_attention_shard_exchange(v, v, v, 0, 10, v, v, v, v, v, 8, 100, 1e-6, v, 2, 0, -1, v, 1 << 30,
+                                           None) == -1
+    assert b'sequence number' in lib.qv_error()

@@ -53,8 +53,8 @@ def _worker(rank, world, port, position, batch, mode, result):
         out = torch.empty((batch, 24, 256), device=dev)
         if mode == 'peer':
             ex = PeerExchange(hot, dist, s)
-            for slot in (0, 1, 0, 1):
-                ex(out, kc, vc, *args, slot)
+            for seq in range(4):
+                ex(out, kc, vc, *args, seq)
         else:
             part, lse = torch.empty((batch, 24, 256), device=dev), torch.empty((batch, 24), device=dev)
             gp, gl = torch.empty((world, batch, 24, 256), device=dev), torch.empty((world, batch, 24), device=dev)

@@ -137,16 +137,23 @@ def _prefill_gpu(hot, q, k, v, position=0):
 
 
 def test_config3_prefill_sampled_rows(hot):
+    """Config 3 (4,096-token causal prefill) against the oracle: every query head on 49 sampled rows
+    (tile edges and random rows), and for every KV head one full 128-row query tile of all six query
+    heads that read it (tiles 31, 0, 16 and 5: the longest, the shortest and two in between)."""
     q, k, v = I.prefill_attention(length=4096)
     out, lse = _prefill_gpu(hot, q, k, v)
     rng = np.random.default_rng(99)
     rows = np.unique(np.concatenate([[0, 1, 63, 64, 127, 128, 2047, 4094, 4095], rng.integers(0, 4096, 40)]))
-    heads = [0, 5, 6, 11, 17, 23]
-    exp, exp_lse = oracle.prefill_attention_core(q, k, v, rows=rows, heads=heads)
-    got = out[rows][:, heads]
+    exp, exp_lse = oracle.prefill_attention_core(q, k, v, rows=rows)
     # fp16 probabilities (FAST mode): the north-star bound, max-abs <= 2e-3.
-    assert np.abs(got - exp).max() <= ATTN_MAX_ABS
-    np.testing.assert_allclose(lse[rows][:, heads], exp_lse, atol=1e-3, rtol=0)
+    assert np.abs(out[rows] - exp).max() <= ATTN_MAX_ABS
+    np.testing.assert_allclose(lse[rows], exp_lse, atol=1e-3, rtol=0)
+    for kv_head, tile in enumerate((31, 0, 16, 5)):
+        tile_rows = np.arange(128 * tile, 128 * tile + 128)
+        heads = list(range(6 * kv_head, 6 * kv_head + 6))
+        exp, exp_lse = oracle.prefill_attention_core(q, k, v, rows=tile_rows, heads=heads)
+        assert np.abs(out[tile_rows][:, heads] - exp).max() <= ATTN_MAX_ABS, (kv_head, tile)
+        np.testing.assert_allclose(lse[tile_rows][:, heads], exp_lse, atol=1e-3, rtol=0)
 
 
 @pytest.mark.parametrize('L,position', [(1000, 0), (200, 77)])
@@ -206,29 +213,23 @@ def test_chunked_delta_against_recurrence(hot, length, with_state):
 
 def test_config4_chunked_prefill_then_verify(hot):
     """Config 4 end to end: a 4,096-token chunked prefill from a zero state, its state handed to 8
-    recurrent verify tokens, checked against the token-by-token CPU recurrence over all 4,104 tokens
-    (value heads 0-15, which use key heads 0-15), and all 48 heads against the recurrent kernel."""
-    import torch
+    recurrent verify tokens (qv_delta_core), every value head checked against the token-by-token
+    fp64 CPU recurrence over all 4,104 tokens: the prefill outputs and state, then the verify
+    outputs and the final state."""
     L = 4096
     c = I.delta_prefill(length=L + 8)
     pre = {k: v[:L] for k, v in c.items()}
     ver = {k: v[L:] for k, v in c.items()}
     out_c, st_c = _delta_chunked_gpu(hot, pre, np.zeros((48, 128, 128), np.float32))
-    out_r, st_r = _delta_core_gpu(hot, pre, np.zeros((48, 128, 128), np.float32))
-    assert rel_err(st_c, st_r) <= DELTA_STATE_REL
-    close(out_c, out_r, 1e-4)
     out_v, st_v = _delta_core_gpu(hot, ver, st_c)
     q, k, g, b = oracle.hotpath.prepare_delta_inputs(c['q'], c['k'], c['alpha'], c['beta'])
-    heads = 16
-    exp_pre, exp_state = oracle.delta_core(np.zeros((heads, 128, 128)), q[:L], k[:L], c['v'][:L, :heads],
-                                           g[:L, :heads], b[:L, :heads])
-    exp_ver, exp_final = oracle.delta_core(exp_state, q[L:], k[L:], c['v'][L:, :heads], g[L:, :heads],
-                                           b[L:, :heads])
-    assert rel_err(st_c[:heads], exp_state) <= DELTA_STATE_REL
-    assert rel_err(st_v[:heads], exp_final) <= DELTA_STATE_REL
-    close(out_c[:, :heads], exp_pre, 1e-4)
-    close(out_v[:, :heads], exp_ver, 1e-4)
-    del torch
+    exp_pre, exp_state = oracle.delta_core(np.zeros((48, 128, 128)), q[:L], k[:L], c['v'][:L], g[:L], b[:L])
+    exp_ver, exp_final = oracle.delta_core(exp_state, q[L:], k[L:], c['v'][L:], g[L:], b[L:])
+    for h in range(48):          # the north-star bound on every head's state, after the prefill and the verify
+        assert rel_err(st_c[h], exp_state[h]) <= DELTA_STATE_REL, h
+        assert rel_err(st_v[h], exp_final[h]) <= DELTA_STATE_REL, h
+    close(out_c, exp_pre, 1e-4)
+    close(out_v, exp_ver, 1e-4)
 
 
 def test_config4_delta_core_against_recurrence(hot):
@@ -285,11 +286,83 @@ def test_peer_exchange_with_a_single_rank_equals_the_layer(hot):
     buf = torch.zeros(nwords, dtype=torch.float32, device=dev)
     peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
     exp_out, _, _ = oracle.attention(**c)
-    for slot in (0, 1, 0):           # consecutive calls alternate the slot
+    for seq in range(3):             # consecutive calls count up
         out = torch.empty((8, 24, 256), device=dev)
         hot.attention_shard_exchange(out, kc, vc, 0, 3000, t('q_gate'), t('key'), t('value'), t('q_norm'),
-                                     t('k_norm'), 8, 3000, peers, 1, 0, slot)
+                                     t('k_norm'), 8, 3000, peers, 1, 0, seq)
         assert hot.status() == 0
         close(out.cpu().numpy().reshape(-1), exp_out, 3e-4)
     flags = buf[nwords - 2 * 240:].view(torch.int32)
     assert int(flags.abs().sum()) == 0, 'consumers reset every flag'
+
+
+def _plant_peer_words(buf, part, lse, world, peer, seq):
+    """Write `peer`'s (partial, LSE) of every row into a receive buffer as the exchange kernel's
+    tagged 64-bit words (low half: the float's bits; high half: 0x51000000 | (seq & 0xFFFFFF)),
+    at buffer slot seq & 1.  Buffer layout: [2 slots][world][240 rows][264 words], row = t*24 + h,
+    words 0..255 the partial, word 256 the LSE."""
+    import torch
+    rows, words = 240, 264
+    tag = np.uint64(0x51000000 | (seq & 0xFFFFFF)) << np.uint64(32)
+    batch = part.shape[0]
+    img = np.zeros((batch * 24, words), np.uint64)
+    img[:, :256] = part.reshape(batch * 24, 256).view(np.uint32).astype(np.uint64) | tag
+    img[:, 256] = lse.reshape(-1).view(np.uint32).astype(np.uint64) | tag
+    view = buf.view(2, world, rows, words)
+    view[seq & 1, peer, :batch * 24] = torch.from_numpy(img.view(np.int64)).to(buf.device)
+
+
+def test_peer_exchange_merges_a_planted_peer_partial(hot):
+    """The two-rank exchange on one GPU: rank 1's (partial, LSE) are planted in rank 0's receive
+    buffer as the words rank 1 would store, so rank 0's kernel finds them without waiting on
+    another kernel.  Rank 0's call must merge them into the full layer's output and zero the words
+    it read.  A planted word with the tag of two calls back is refused: the bounded wait gives up
+    and qv_status reports the timeout, and the next call on the same buffers is correct again."""
+    import torch
+    from redshift_b200.sharding import plan, shard_capacity
+    batch, position, world = 8, 3000, 2
+    c = I.attention_layer(batch=batch, position=position, seed=4200)
+    dev = torch.device('cuda')
+    t = lambda k: torch.from_numpy(np.ascontiguousarray(np.asarray(c[k], np.float32))).to(dev)  # noqa: E731
+    args = (t('q_gate'), t('key'), t('value'), t('q_norm'), t('k_norm'))
+    caches = []
+    for rank in range(world):
+        s = plan(position, world, rank, batch)
+        kc = torch.zeros((shard_capacity(s, batch), 4, 256), dtype=torch.float16, device=dev)
+        vc = torch.zeros_like(kc)
+        kc[:s.rows] = torch.from_numpy(c['key_cache'][s.begin:s.begin + s.rows]).to(dev)
+        vc[:s.rows] = torch.from_numpy(c['value_cache'][s.begin:s.begin + s.rows]).to(dev)
+        caches.append((s, kc, vc))
+    s1, kc1, vc1 = caches[1]
+    part1 = torch.empty((batch, 24, 256), device=dev)
+    lse1 = torch.empty((batch, 24), device=dev)
+    hot.attention_shard(part1, lse1, kc1, vc1, s1.begin, s1.rows, *args, batch, position)
+    part1, lse1 = part1.cpu().numpy(), lse1.cpu().numpy()
+    nwords = hot.lib.qv_attention_exchange_bytes(world) // 8
+    bufs = [torch.zeros(nwords, dtype=torch.int64, device=dev) for _ in range(world)]
+    peers = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=dev)
+    s0, kc0, vc0 = caches[0]
+    exp_out, _, _ = oracle.attention(**c)
+
+    def call(seq):
+        out = torch.full((batch, 24, 256), float('nan'), device=dev)
+        hot.attention_shard_exchange(out, kc0, vc0, s0.begin, s0.rows, *args, batch, position, peers, world, 0,
+                                     seq)
+        return out, hot.status()
+
+    for seq in (5, 6):
+        _plant_peer_words(bufs[0], part1, lse1, world, 1, seq)
+        out, status = call(seq)
+        assert status == 0
+        got = out.cpu().numpy().reshape(-1)
+        assert np.abs(got - exp_out).max() <= ATTN_MAX_ABS
+        close(got, exp_out, 3e-4)
+        assert int(bufs[0].view(2, world, 240, 264)[seq & 1, 1].abs().sum()) == 0, 'read words are zeroed'
+    # a leftover word from call 5 in slot 1 (two calls before 7) must not be taken for call 7's data
+    _plant_peer_words(bufs[0], part1, lse1, world, 1, 5)
+    _, status = call(7)
+    assert status == 1, 'the stale words are refused and the bounded wait reports a timeout'
+    _plant_peer_words(bufs[0], part1, lse1, world, 1, 8)
+    out, status = call(8)
+    assert status == 0
+    close(out.cpu().numpy().reshape(-1), exp_out, 3e-4)

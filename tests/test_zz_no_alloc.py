@@ -15,6 +15,7 @@ import ctypes as ct
 import numpy as np
 import pytest
 
+import oracle
 from oracle import inputs as I
 
 pytestmark = pytest.mark.gpu
@@ -58,6 +59,9 @@ def test_no_alloc_matches_the_workspace_entry_point_twice_in_a_row(lib):
         bad = np.abs(out_a - out_b) > 3e-4 * (1 + np.abs(out_b))
         assert not bad.any()
         assert np.array_equal(k_a, k_b) and np.array_equal(v_a, v_b)
+        # and both against the CPU oracle (max-abs <= 2e-3)
+        expected, _, _ = oracle.attention(**case)
+        assert np.abs(out_a.reshape(-1) - expected).max() <= 2e-3
 
 
 def test_no_alloc_rejects_batches_beyond_the_fixed_scratch(lib):
