@@ -179,8 +179,8 @@ class Step:
             self.glse = torch.empty((world, tokens, H), **f32)
         else:
             need = hot.lib.qv_attention_workspace(tokens, self.position)
-        self.ws = torch.empty(max(int(need), 256), dtype=torch.uint8, device=self.dev)
-        self.launches_per_step = len(self.attn) * 2 + len(self.delta)   # fused attention + combine/exchange
+        self.ws = torch.zeros(max(int(need), 256), dtype=torch.uint8, device=self.dev)   # barrier words start at 0
+        self.launches_per_step = len(self.attn) + len(self.delta)   # one launch per layer (split combine / exchange in the tail)
 
     def use_peer_exchange(self, dist):
         """Switch the N>1 attention layers to the fused peer-memory exchange."""
@@ -326,8 +326,8 @@ def bench_b200(args):
                 exchange = 'fused peer-memory exchange (P2P stores + flags, symmetric memory)'
             except Exception as exc:
                 print(f'# peer exchange unavailable ({exc}); using NCCL all-gather', file=sys.stderr)
-        if step.exchange is None:       # shard + combine + merge kernels per attention layer
-            step.launches_per_step = len(step.attn) * 3 + len(step.delta)   # + shard combine + merge
+        if step.exchange is None:       # shard kernel + merge kernel per attention layer
+            step.launches_per_step = len(step.attn) * 2 + len(step.delta)
     torch.cuda.synchronize()
 
     def barrier():
@@ -427,8 +427,8 @@ def bench_b200(args):
     roofline = {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': hbm_peak, 'unit': 'GB/s',
                 'frac': round(achieved / hbm_peak, 4),
                 'traffic': FA_TRAFFIC_139K if (args.context == 139264 and world == 1) else None,
-                'kernel': 'attention layer (split-KV fa_kernel with fused prepare/append + combine or exchange), '
-                          'per rank',
+                'kernel': 'attention layer (one split-KV fa_kernel launch: prepare/append, attention, split '
+                          'combine or peer exchange in its tail), per rank',
                 'algorithmic_bytes_per_launch': attn_bytes, 'avg_layer_ms': round(attn_ms, 5),
                 'peak_source': peak_kind}
 
@@ -480,19 +480,21 @@ def bench_b200(args):
 def side_measurements(hot, torch, tc_peak, hbm_peak):
     """Attention at 32k, causal prefill (config 3) and DeltaNet prefill core (config 4)."""
     res = {}
-    # config 2 at 32,768
+    # config 2 at 32,768: the 16 attention layers of a step back to back, replayed as a
+    # CUDA graph (eager launches from Python would leave the GPU waiting on the host)
     step = Step(hot, 32768, 8, 0, 1, seed=77)
-    a = step.attn[0]
+    graph = capture(torch, lambda: [step.attention_layer(a) for a in step.attn])
     for _ in range(3):
-        step.attention_layer(a)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(20)]
-    for i in range(20):
-        a = step.attn[i % 16]
-        ev[i][0].record()
-        step.attention_layer(a)
-        ev[i][1].record()
+        graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        graph.replay()
+    e1.record()
     torch.cuda.synchronize()
-    ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
+    ms = e0.elapsed_time(e1) / (10 * len(step.attn))
+    graph.reset()
+    del graph
     res['attention_32k_us'] = round(ms * 1e3, 2)
     res['attention_32k_hbm_frac'] = round(32768 * 4096 / (ms * 1e-3) / 1e9 / hbm_peak, 4)
     del step

@@ -104,7 +104,11 @@ int qv_test_delta_prefill(float *out, float *state, float *history,
  * src/runtime.cu:402-405).  All pointers are device memory; the call is
  * asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream).
  * The caches hold >= position+batch rows.  `workspace` is caller-owned device
- * memory of at least qv_attention_workspace(batch, position) bytes. */
+ * memory of at least qv_attention_workspace(batch, position) bytes; it must
+ * be zero-filled once before its first use (its first 256 bytes hold the
+ * counters of the barrier at which a decode launch's CTAs meet before they
+ * combine their splits; every call leaves them ready for the next, so later
+ * calls need no clearing).  A workspace serves one call at a time. */
 size_t qv_attention_workspace(int batch, int position);
 int qv_attention(float *out, void *key_cache, void *value_cache,
                  const float *q_gate, const float *key, const float *value,
@@ -185,7 +189,8 @@ int qv_delta_commit(float *state, float *history, const float *saved_state,
  * partial [batch,24,256] (no gate) and natural-log LSE [batch,24] (-inf for
  * rows that see no key).  batch 1..10.  qv_attention_merge combines `shards`
  * stacked partials [shards,batch,24,256] / LSEs [shards,batch,24] into the
- * gated output [batch,24,256]. */
+ * gated output [batch,24,256].  The workspace follows qv_attention's rule
+ * (zero-filled before its first use). */
 size_t qv_attention_shard_workspace(int batch, int shard_rows);
 int qv_attention_shard(float *partial, float *lse, void *key_cache, void *value_cache,
                        int shard_begin, int shard_rows,
@@ -266,10 +271,13 @@ int qv_delta_chunked(float *out, float *state, const void *q, const void *k, con
  * asynchronous on `stream`), with batch limited to 1..8.
  * The first call on a device looks up the array's device address (once per
  * device, with that device current); make that first call before any stream
- * capture.  Every call uses the same array and leaves its contents behind;
- * nothing in it has to start at zero, as each call writes every scratch byte
- * it reads.  Calls that overlap on the GPU (other streams, other host
- * threads) race on the array: issue them in order on one stream per device. */
+ * capture.  Every call uses the same array and leaves its contents behind.
+ * The array is zero when the library loads; its first 256 bytes are the
+ * counters of the barrier inside the attention launch, which must start at
+ * zero and which every call leaves at zero again, and each call writes every
+ * other byte before reading it.  Calls that overlap on the GPU (other
+ * streams, other host threads) race on the array: issue them in order on one
+ * stream per device. */
 int qv_attention_noalloc(float *out, void *key_cache, void *value_cache,
                          const float *q_gate, const float *key, const float *value,
                          const float *q_norm, const float *k_norm,

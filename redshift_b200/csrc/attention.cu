@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "hotpath.h"
 
+#include <algorithm>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdexcept>
@@ -98,20 +99,31 @@ __device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_
 // TMEM columns: S double buffer [0,128), O [128,384), Q (A operand) [384,512).
 constexpr uint32_t TM_S = 0, TM_O = 128, TM_Q = 384;
 
+// What a decode launch does with its rows once every split is done (the
+// kernel tail, after a barrier over the CTAs of each KV head).
+enum DecodeTail : int {
+    TAIL_GATED = 0,      // out = softmax(...) V * sigmoid(gate)
+    TAIL_SHARD = 1,      // out = normalised partial of this cache shard, lse = its natural-log LSE
+    TAIL_EXCHANGE = 2,   // shard partial pushed to every rank's buffer, all ranks' partials merged, gated
+};
+
 struct FaParams {
     const __half *q;        // prepared queries [T][24][256] (fp16 of q)
     const __half *q_lo;     // fp16 of (q - fp16(q)) (PRECISE)
-    const float *q_gate;    // [T][24][512], gate = [256:512) (direct mode), may be null
-    float *out;             // [T][24][256] (direct mode)
-    float *lse;             // optional natural-log LSE [T][24] (direct mode)
-    float *part_o;          // [4][splits][64][256] unnormalised partial O (split mode)
-    float *part_ml;         // [4][splits][64][2]  (running max in log2 units, sum)
+    const float *q_gate;    // [T][24][512], gate = [256:512), may be null (core prefill)
+    float *out;             // [T][24][256]
+    float *lse;             // natural-log LSE [T][24] (prefill: optional; decode: TAIL_SHARD)
+    float *part_o;          // decode: [4][64 rows][splits][256] unnormalised partial O of every split
+    float *part_ml;         // decode: [4][64 rows][MAXS][2] (running max in log2 units, sum)
+    unsigned long long *sync;  // decode: [4] per-KV-head barrier words (generation : arrivals)
     int T, position;        // tokens and absolute position of token 0
     int kv_begin;           // absolute position of cache row 0
     int kv_rows;            // valid cache rows
-    int mode;               // 0 = decode (GQA-packed rows), 1 = prefill (head-major rows)
+    int mode;               // 0 = decode (GQA-packed rows, split-KV), 1 = prefill (head-major rows)
     int split_tiles, splits;
-    int direct;             // 1: write final output; 0: write split partials
+    int tail;               // decode: DecodeTail
+    const uint64_t *peers;  // TAIL_EXCHANGE: every rank's receive buffer
+    int world, rank, seq;
     // Decode with the prepare step folded in (fused = 1): the CTA normalises
     // and rotates its own query rows from q_gate and, when its tiles hold the
     // block's new cache rows, writes their keys / values before loading them.
@@ -141,6 +153,272 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volati
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
 }
 
+// ---------------------------------------------------------------- decode tail
+// After its split of the cache, a decode CTA waits at a barrier over the CTAs
+// of its KV head, then combines a share of the head's rows from all splits'
+// partials (rows blockIdx.x, blockIdx.x + splits, ...): the split combine
+// runs inside the attention launch, on every SM, with no second kernel.
+constexpr float LN2 = 0.6931471805599453f;
+constexpr int MAXS = 40;                               // splits a tail combine handles (plans use <= 37)
+
+// Peer exchange (TAIL_EXCHANGE, multi-GPU verify).  Each rank's receive
+// buffer holds [2 slots][world][EX_ROWS][EX_WORDS] 64-bit words (256 O, lse,
+// padding) per row t*24 + h.  Every value travels as a word {value bits,
+// tag}: the reader spins on each of its words until the tag of this call
+// appears, so no fence or separate flag write is needed, and it zeroes each
+// word after reading it.  `seq` counts the calls on these buffers (the same
+// on every rank, +1 per call): its parity picks the slot and its low 24 bits
+// are in the tag.  A rank writes into a slot again two calls later, after it
+// has received this rank's partials of the call in between, and that call
+// started only after this one (and its zeroing) completed.  A word that
+// arrives after its reader gave up (a timeout) stays behind unread, but it
+// carries the tag of its own call and the next call on that slot waits for a
+// different tag, so it is never taken for new data.
+constexpr int EX_ROWS = MAX_DECODE_T * NQ;       // rows of the largest decode batch
+constexpr int EX_WORDS = 264;                    // words per row: 256 O + lse, padded to 64 bytes
+constexpr int EX_MAX_WORLD = 8;
+__host__ __device__ constexpr uint32_t ex_tag(int seq) {   // high half of a filled word; never 0
+    return 0x51000000u | ((uint32_t)seq & 0x00FFFFFFu);
+}
+__host__ __device__ constexpr size_t ex_bytes(int world) {
+    return (size_t)2 * world * EX_ROWS * EX_WORDS * sizeof(uint64_t);
+}
+
+// Barrier over the `splits` CTAs of one KV head, on one 64-bit word of the
+// workspace: arrivals in the low half, a generation count in the high half.
+// The arrivals must be zero before the first launch on a workspace.  A CTA
+// waits until the arrivals reach `splits` or the generation moves on; the
+// last CTA to arrive then resets the arrivals and advances the generation in
+// one atomic add (off the others' critical path: they may leave as soon as
+// its arrival shows), so every launch leaves the arrivals zero, also after a
+// timeout (every CTA arrives; only a waiter gives up).  A launch has at most
+// (SMs / 4) CTAs per head and one CTA per SM, so all CTAs of a head are
+// resident together.  Bounded: a wait past the limit raises STATUS_TIMEOUT.
+__device__ bool head_barrier(unsigned long long *word, int splits, volatile int *flag) {
+    fence_async_global();                              // the partials are read back by bulk copies
+    __syncthreads();                                   // this CTA's partials are written
+    if (threadIdx.x == 0) {
+        __threadfence();                               // release them
+        const unsigned long long old = atomicAdd(word, 1ull);
+        bool ok = true;
+        if ((uint32_t)old == (uint32_t)splits - 1) {
+            atomicAdd(word, (1ull << 32) - (unsigned long long)splits);   // arrivals -> 0, generation + 1
+        } else {
+            const uint32_t gen = (uint32_t)(old >> 32);
+            const long long start = clock64();
+            while (true) {
+                const unsigned long long v = ld_acquire_gpu_u64(word);
+                if ((uint32_t)v >= (uint32_t)splits || (uint32_t)(v >> 32) != gen) break;
+                if (clock64() - start > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok = false; break; }
+            }
+        }
+        __threadfence();                               // acquire the other CTAs' partials
+        *flag = ok ? 1 : 0;
+    }
+    __syncthreads();
+    return *flag != 0;
+}
+
+// Bulk copy global -> shared (no tensor map), completion on the mbarrier's
+// transaction count: addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
+
+// Split combine of decode rows ra and rb (rb < 0: ra only) of KV head g (row r
+// = token r / 6, head 6g + r % 6).  A row's partials of all splits are one
+// contiguous block (splits x 1 KB), and so are its splits' (max, sum) pairs
+// (MAXS x 8 bytes): thread 0 brings both rows' blocks into shared memory
+// (`buf`, the idle K/V ring) with bulk copies on `bar` (phase parity
+// `phase`).  o[k] receives the normalised value of row k in dimension
+// threadIdx.x, lse[k] its natural-log LSE.  `sh` holds 2 MAXS + 8 floats of
+// shared memory; the call ends with a CTA barrier.
+__device__ bool combine_rows(const FaParams &p, int g, int ra, int rb, float *sh, float *buf, uint64_t *bar,
+                             uint32_t phase, volatile int *abort_flag, float (&o)[2], float (&lse)[2]) {
+    const int d = threadIdx.x, S = p.splits;
+    const bool two = rb >= 0;
+    const size_t row_a = (size_t)g * DECODE_ROWS + ra, row_b = (size_t)g * DECODE_ROWS + (two ? rb : ra);
+    float *xa = buf, *xb = buf + (size_t)S * HD;                    // partials [split][256]
+    float *mla = buf + 2 * (size_t)S * HD, *mlb = mla + 2 * MAXS;   // (max, sum) [MAXS][2]
+    if (threadIdx.x == 0) {
+        // The partials were written through the generic proxy (and acquired
+        // at the barrier); the bulk copies read them through the async proxy,
+        // and overwrite shared memory the CTA last used through the generic one.
+        fence_async_global();
+        fence_async_shared();
+        const uint32_t bytes = (uint32_t)S * HD * sizeof(float), ml_bytes = 2 * MAXS * sizeof(float);
+        mbar_expect_tx(bar, two ? 2 * (bytes + ml_bytes) : bytes + ml_bytes);
+        bulk_load(xa, p.part_o + row_a * S * HD, bytes, bar);
+        bulk_load(mla, p.part_ml + row_a * 2 * MAXS, ml_bytes, bar);
+        if (two) {
+            bulk_load(xb, p.part_o + row_b * S * HD, bytes, bar);
+            bulk_load(mlb, p.part_ml + row_b * 2 * MAXS, ml_bytes, bar);
+        }
+    }
+    const bool ok = mbar_wait(bar, phase, abort_flag);
+    // (max, sum) of split e of row a on threads [0, S), of row b on [64, 64 + S)
+    const int e = d < 64 ? d : d - 64;
+    float m = -INFINITY, l = 0.f;
+    if (ok && e < S && (d < 64 || (two && d < 128))) {
+        const float *ml = d < 64 ? mla : mlb;
+        m = ml[2 * e]; l = ml[2 * e + 1];
+    }
+    float *wa = sh, *wb = sh + MAXS, *red = sh + 2 * MAXS;   // red: maxima [0..3], sums [4..7]
+    float M = m;
+#pragma unroll
+    for (int k = 16; k; k >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, k));
+    if (d < 128 && (d & 31) == 0) red[d >> 5] = M;
+    __syncthreads();
+    const float Ma = fmaxf(red[0], red[1]), Mb = fmaxf(red[2], red[3]);
+    const float w = (e < S && d < 128 && m != -INFINITY) ? exp2f(m - (d < 64 ? Ma : Mb)) : 0.f;
+    if (d < MAXS) wa[d] = w;
+    else if (d >= 64 && d < 64 + MAXS) wb[d - 64] = w;
+    const float den_part = warp_sum(w * l);
+    if (d < 128 && (d & 31) == 0) red[4 + (d >> 5)] = den_part;
+    __syncthreads();
+    const float den_a = red[4] + red[5], den_b = red[6] + red[7];
+    float aa[4] = {0.f, 0.f, 0.f, 0.f}, ab[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+        for (int k = 0; k < S; ++k) aa[k & 3] += wa[k] * xa[(size_t)k * HD + d];
+        if (two)
+            for (int k = 0; k < S; ++k) ab[k & 3] += wb[k] * xb[(size_t)k * HD + d];
+    }
+    o[0] = den_a > 0.f ? ((aa[0] + aa[1]) + (aa[2] + aa[3])) / den_a : 0.f;
+    o[1] = den_b > 0.f ? ((ab[0] + ab[1]) + (ab[2] + ab[3])) / den_b : 0.f;
+    lse[0] = den_a > 0.f ? (Ma + log2f(den_a)) * LN2 : -INFINITY;
+    lse[1] = den_b > 0.f ? (Mb + log2f(den_b)) * LN2 : -INFINITY;
+    __syncthreads();                                   // sh and buf are free again
+    return ok;
+}
+
+// Peer exchange of up to two rows (global row indices grow[k] = t*24 + h, k <
+// nr): this shard's normalised values o[k] (dimension threadIdx.x) and LSEs go
+// into slot [rank] of every other rank's buffer, then the other ranks' words
+// of the rows are read from this rank's own buffer (all peers and both rows
+// at once, so their latencies overlap; a word without this call's tag is
+// re-read until it has it, bounded) and merged: sum_g exp(lse_g - LSE) o_g,
+// written back into o[k].  `sh` holds 2 EX_MAX_WORLD floats; the call ends
+// with a CTA barrier.
+__device__ void exchange_rows(const FaParams &p, const int (&grow)[2], int nr, float (&o)[2], const float (&lse)[2],
+                              float *sh) {
+    const int d = threadIdx.x, world = p.world, rank = p.rank, slot = p.seq & 1;
+    const uint32_t tag32 = ex_tag(p.seq);
+    const uint64_t tag = (uint64_t)tag32 << 32;
+    for (int k = 0; k < nr; ++k)
+        for (int q = 0; q < world; ++q) {
+            if (q == rank) continue;
+            uint64_t *dst = reinterpret_cast<uint64_t *>(p.peers[q]) +
+                            (((size_t)slot * world + rank) * EX_ROWS + grow[k]) * EX_WORDS;
+            st_word_sys(dst + d, tag | __float_as_uint(o[k]));
+            if (d == 0) st_word_sys(dst + HD, tag | __float_as_uint(lse[k]));
+        }
+    uint64_t *own = reinterpret_cast<uint64_t *>(p.peers[rank]);
+    auto word_of = [&](int q, int k, int col) {
+        return own + (((size_t)slot * world + q) * EX_ROWS + grow[k]) * EX_WORDS + col;
+    };
+    const long long t0 = clock64();
+    bool ok = true;
+    auto finish = [&](uint64_t *word, uint64_t x, float fallback) {
+        while ((uint32_t)(x >> 32) != tag32) {
+            if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok = false; return fallback; }
+            x = ld_word_sys(word);
+        }
+        *word = 0;
+        return __uint_as_float((uint32_t)x);
+    };
+    // LSE words: peer q of row k on thread 32k + q
+    const int lk = d >> 5, lq = d & 31;
+    const bool lse_reader = lk < nr && lq < world && lq != rank;
+    const uint64_t lse_first = lse_reader ? ld_word_sys(word_of(lq, lk, HD)) : 0;
+    uint64_t first[2][EX_MAX_WORLD];
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+        for (int q = 0; q < EX_MAX_WORLD; ++q)
+            first[k][q] = (k < nr && q < world && q != rank) ? ld_word_sys(word_of(q, k, d)) : 0;
+    if (lk < nr && lq < world) sh[lk * EX_MAX_WORLD + lq] = lse_reader ? finish(word_of(lq, lk, HD), lse_first, 0.f) : lse[lk];
+    float val[2][EX_MAX_WORLD];
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+        for (int q = 0; q < EX_MAX_WORLD; ++q) {
+            val[k][q] = 0.f;
+            if (k < nr && q < world) val[k][q] = q == rank ? o[k] : finish(word_of(q, k, d), first[k][q], 0.f);
+        }
+    const int all_ok = __syncthreads_and(ok);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        float res = 0.f;
+        if (all_ok && k < nr) {
+            const float *ls = sh + k * EX_MAX_WORLD;
+            float Mx = -INFINITY;
+            for (int q = 0; q < world; ++q) Mx = fmaxf(Mx, ls[q]);
+            float num = 0.f, den = 0.f;
+            if (Mx != -INFINITY) {
+#pragma unroll
+                for (int q = 0; q < EX_MAX_WORLD; ++q) {
+                    if (q >= world || ls[q] == -INFINITY) continue;
+                    const float wq = expf(ls[q] - Mx);
+                    den += wq;
+                    num += wq * val[k][q];
+                }
+            }
+            res = den > 0.f ? num / den : 0.f;
+        }
+        o[k] = res;
+    }
+    __syncthreads();                                   // sh is free again
+}
+
+// The decode tail of one CTA (all 256 threads): barrier over the KV head,
+// then this CTA's rows of the head (blockIdx.x, blockIdx.x + splits, ...),
+// two at a time, combined and written as p.tail says.  `scratch` is a little
+// shared memory, `buf` room for two rows' partials of every split, `bar` an
+// mbarrier (count 1) that no earlier phase of this launch used.
+__device__ void decode_tail(const FaParams &p, int g, uint8_t *scratch, float *buf, uint64_t *bar,
+                            volatile int *abort_flag) {
+    float *sh = reinterpret_cast<float *>(scratch);
+    volatile int *flag = reinterpret_cast<volatile int *>(sh + 2 * MAXS + 8 + 2 * EX_MAX_WORLD);
+    const int nrows = p.T * GROUP, d = threadIdx.x;
+    auto global_row = [&](int r) { return (r / GROUP) * NQ + g * GROUP + r % GROUP; };
+    // The gates of this CTA's first two rows load while the CTA waits at the barrier.
+    auto load_gates = [&](int ra, int rb, float (&gate)[2]) {
+        gate[0] = gate[1] = 0.f;
+        if (p.tail == TAIL_SHARD) return;
+        if (ra < nrows) gate[0] = p.q_gate[(size_t)global_row(ra) * 2 * HD + HD + d];
+        if (rb >= 0) gate[1] = p.q_gate[(size_t)global_row(rb) * 2 * HD + HD + d];
+    };
+    float gate[2];
+    {
+        const int ra = blockIdx.x, rb = ra + p.splits < nrows ? ra + p.splits : -1;
+        load_gates(ra, rb, gate);
+    }
+    if (!head_barrier(p.sync + g, p.splits, flag)) return;
+    if (threadIdx.x == 0) QV_STAMP(7);
+    uint32_t phase = 0;
+    for (int ra = blockIdx.x; ra < nrows; ra += 2 * p.splits, phase ^= 1) {
+        const int rb = ra + p.splits < nrows ? ra + p.splits : -1;
+        const int nr = rb >= 0 ? 2 : 1;
+        if (ra != (int)blockIdx.x) load_gates(ra, rb, gate);
+        float o[2], lse[2];
+        if (!combine_rows(p, g, ra, rb, sh, buf, bar, phase, abort_flag, o, lse)) return;
+        const int grow[2] = {global_row(ra), nr == 2 ? global_row(rb) : 0};
+        if (p.tail == TAIL_EXCHANGE) exchange_rows(p, grow, nr, o, lse, sh + 2 * MAXS + 8);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            if (k >= nr) break;
+            if (p.tail == TAIL_SHARD) {
+                p.out[(size_t)grow[k] * HD + d] = o[k];
+                if (d == 0) p.lse[grow[k]] = lse[k];
+            } else {
+                p.out[(size_t)grow[k] * HD + d] = o[k] * sigmoidf_(gate[k]);
+            }
+        }
+    }
+    if (threadIdx.x == 0) QV_STAMP(8);
+}
+
 template <bool PRECISE>
 __global__ void __launch_bounds__(PRECISE ? 256 : 384, 1)
 fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -153,11 +431,12 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         if (threadIdx.x == 0) raise_status(STATUS_BAD_ARGUMENT);
         return;
     }
+    if (threadIdx.x == 0) QV_STAMP(0);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::SM_BAR);
     uint64_t *k_full = bars, *v_full = bars + 3, *k_empty = bars + 6, *v_empty = bars + 9,
              *s_full = bars + 12, *s_free = bars + 14, *p_full = bars + 16, *p_free = bars + 18,
              *mma_done = bars + 20, *q_ready = bars + 21, *app_done = bars + 22, *xbar = bars + 23,
-             *lbar = bars + 25;
+             *lbar = bars + 25, *cbar = bars + 26;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::SM_BAR + 224);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::SM_BAR + 228);
     float2 *rope = reinterpret_cast<float2 *>(smem + L::SM_ROPE);
@@ -187,6 +466,17 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     const bool appends = app_hi > app_lo;
     const int app_tile = appends ? app_lo / BN - tile0 : ntiles;    // first tile holding a new row
 
+    // Fused decode, before anything else: L2 prefetch hints for this CTA's
+    // query rows (the q half of q_gate), so that their HBM latency overlaps
+    // the previous kernel's tail.  (Prefetching K/V tiles as well measured
+    // slower: the extra traffic delays the query loads and thrashes L2.)
+    if (PRECISE && p.fused) {
+        for (int i = threadIdx.x; i < p.T * GROUP * 8; i += blockDim.x) {    // 8 lines of 128 B per row
+            const int rr = i >> 3;
+            prefetch_l2(p.q_gate + ((size_t)(rr / GROUP) * NQ + kv_head * GROUP + rr % GROUP) * 2 * HD + (i & 7) * 32);
+        }
+    }
+
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES3; ++i) {
             mbar_init(k_full + i, 1); mbar_init(v_full + i, 1);
@@ -200,6 +490,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         mbar_init(mma_done, 1);
         mbar_init(q_ready, p.fused ? 8 : 4);      // every warp (fused) or softmax warps 4-7
         mbar_init(lbar, 4);
+        mbar_init(cbar, 1);
         mbar_init(app_done, 64);
         *abort_flag = 0;
         fence_barrier_init();
@@ -225,14 +516,20 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
 
     // Everything below may read what the previous kernel of the stream wrote.
     grid_dependency_wait();
-    if (threadIdx.x == 0) launch_dependents();
+    if (threadIdx.x == 0) { launch_dependents(); QV_STAMP(1); }
 
-    // Fused decode: tiles 0 and 1 (stages 0 and 1) go out before the queries
-    // are prepared, unless they hold new rows, which must be written first;
-    // stage 2 stages the queries, so tile 2 waits for them.
-    const int early = (PRECISE && p.fused) ? min(ntiles, min(app_tile, 2)) : 0;
-    if (threadIdx.x == 0) {
-        for (int j = 0; j < early; ++j) {
+    // Fused decode: the query rows and norm weights are loaded first (from
+    // L2, ahead of the bulk K/V data, which would otherwise queue in front of
+    // them on the way into the SM); once warp 0's rows have arrived, tiles
+    // 0..2 (all three stages) go out, unless they hold new rows, which must be
+    // written first, and the preparation overlaps their loads.
+    const int early = (PRECISE && p.fused) ? min(ntiles, min(app_tile, STAGES3)) : 0;
+#ifndef QV_TILES_FIRST
+#define QV_TILES_FIRST 0
+#endif
+    const int first_tiles = min(early, QV_TILES_FIRST);      // tiles issued ahead of the query loads
+    auto issue_early = [&](int j0, int j1) {
+        for (int j = j0; j < j1; ++j) {
             uint8_t *kd = smem + L::SM_KV + j * L::SM_KV_STAGE, *vd = kd + TILE_BYTES;
             const int y = (tile0 + j) * BN;
             mbar_expect_tx(k_full + j, TILE_BYTES);
@@ -240,22 +537,12 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             mbar_expect_tx(v_full + j, TILE_BYTES);
             for (int c = 0; c < 4; ++c) tma_load_2d(vd + c * BN * 128, &tmV, v_full + j, kv_head * HD + c * 64, y);
         }
-    }
-
+        QV_STAMP(2);
+    };
+    if (threadIdx.x == 0) issue_early(0, first_tiles);
+    constexpr int QR = DECODE_ROWS / 8;
+    float4 xa[QR], xb[QR], n0, n1;
     if (PRECISE && p.fused) {
-        // ---------------------------------------- fused prepare (all warps)
-        // Query rows r = warp + 8j: RMSNorm with weight, rotary on dims
-        // [0,64), split into fp16 hi + lo (hi: the value truncated to fp16's
-        // 11 significant bits, so that lo = x - hi is exact), written in TMEM
-        // A-row order (hi of row 16g+i at A row 32g+i, lo at 32g+16+i; 512 bytes
-        // per A row, 16-byte chunks XOR-swizzled by the row's low 3 bits) into
-        // the third K/V stage, which the producer leaves idle until the
-        // queries are staged (tiles 0 and 1 are already on their way).  Each warp then copies half the columns of its
-        // TMEM lane quarter; warps 2-3 finally write the block's new keys /
-        // values, if this CTA's tiles hold them.  Lane l of a row holds dims
-        // [4l,4l+4) and [128+4l,128+4l+4).
-        constexpr int QR = DECODE_ROWS / 8;
-        float4 xa[QR], xb[QR];
 #pragma unroll
         for (int j = 0; j < QR; ++j) {
             const int rr = warp + 8 * j;
@@ -267,29 +554,46 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 xa[j] = xb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
+        n0 = *reinterpret_cast<const float4 *>(p.qn + 4 * lane);
+        n1 = *reinterpret_cast<const float4 *>(p.qn + 128 + 4 * lane);
+    }
+
+    if (PRECISE && p.fused) {
+        // ---------------------------------------- fused prepare (all warps)
+        // Query rows r = warp + 8j: RMSNorm with weight, rotary on dims
+        // [0,64), split into fp16 hi + lo (hi: the value truncated to fp16's
+        // 11 significant bits, so that lo = x - hi is exact), placed in TMEM
+        // A-row order (hi of row 16g+i at A row 32g+i, lo at 32g+16+i).  The
+        // rows go to TMEM through the two P buffers (idle until the first
+        // softmax, which needs these queries), in two rounds of 64 columns:
+        // dims [0,128) then [128,256).  A staged A row is 256 bytes, 16-byte
+        // chunks XOR-swizzled by the row's low 3 bits; in each round every
+        // warp copies half the columns of its TMEM lane quarter.  Warps 2-3
+        // finally write the block's new keys / values, if this CTA's tiles
+        // hold them.  Lane l of a row holds dims [4l,4l+4) and [128+4l,128+4l+4).
         // Rotary (cos, sin) of every (token, dim pair) while the loads are in flight.
         for (int e = threadIdx.x; e < p.T * 32; e += 256) rope[e] = rope_angle(p.position + (e >> 5), e & 31);
-        named_barrier(1, 256);
-        const float4 n0 = *reinterpret_cast<const float4 *>(p.qn + 4 * lane);
-        const float4 n1 = *reinterpret_cast<const float4 *>(p.qn + 128 + 4 * lane);
         float ss[QR];
 #pragma unroll
         for (int j = 0; j < QR; ++j)
             ss[j] = xa[j].x * xa[j].x + xa[j].y * xa[j].y + xa[j].z * xa[j].z + xa[j].w * xa[j].w +
                     xb[j].x * xb[j].x + xb[j].y * xb[j].y + xb[j].z * xb[j].z + xb[j].w * xb[j].w;
+        named_barrier(1, 256);                                    // the rotary table is complete
+        // Every warp has its query rows by now (it summed their squares before
+        // the barrier), so the K/V tiles no longer queue in front of them.
+        if (threadIdx.x == 0) issue_early(first_tiles, early);
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
 #pragma unroll
             for (int j = 0; j < QR; ++j) ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], o);
         }
-        uint8_t *qstage = smem + L::SM_KV + 2 * L::SM_KV_STAGE;     // third K/V stage
-        const int sub = (lane & 1) * 8;
         auto split = [](float a, float b, uint32_t &hi, uint32_t &lo) {
             const float ha = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
             const float hb = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
             hi = half2_bits(__floats2half2_rn(ha, hb));
             lo = half2_bits(__floats2half2_rn(a - ha, b - hb));
         };
+        uint32_t hw[QR][2][4];                    // [row][round] {hi0, hi1, lo0, lo1}
 #pragma unroll
         for (int j = 0; j < QR; ++j) {
             const int rr = warp + 8 * j;
@@ -299,37 +603,44 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             float x0[4] = {a.x * inv * n0.x, a.y * inv * n0.y, a.z * inv * n0.z, a.w * inv * n0.w};
             const float x1[4] = {b.x * inv * n1.x, b.y * inv * n1.y, b.z * inv * n1.z, b.w * inv * n1.w};
             rope_row(x0, rope + (live ? rr / GROUP : 0) * 32, lane, live);
-            uint32_t h0, h1, g0, g1, l0, l1, m0, m1;
-            split(x0[0], x0[1], h0, l0);
-            split(x0[2], x0[3], h1, l1);
-            split(x1[0], x1[1], g0, m0);
-            split(x1[2], x1[3], g1, m1);
-            const int ahi = 32 * (rr >> 4) + (rr & 15), sw = ahi & 7;
-            uint8_t *hrow = qstage + ahi * 512, *lrow = hrow + 16 * 512;
-            const int p0 = (((lane >> 1) ^ sw) << 4) + sub, p1 = (((16 + (lane >> 1)) ^ sw) << 4) + sub;
-            *reinterpret_cast<uint2 *>(hrow + p0) = make_uint2(h0, h1);
-            *reinterpret_cast<uint2 *>(hrow + p1) = make_uint2(g0, g1);
-            *reinterpret_cast<uint2 *>(lrow + p0) = make_uint2(l0, l1);
-            *reinterpret_cast<uint2 *>(lrow + p1) = make_uint2(m0, m1);
+            split(x0[0], x0[1], hw[j][0][0], hw[j][0][2]);
+            split(x0[2], x0[3], hw[j][0][1], hw[j][0][3]);
+            split(x1[0], x1[1], hw[j][1][0], hw[j][1][2]);
+            split(x1[2], x1[3], hw[j][1][1], hw[j][1][3]);
         }
-        named_barrier(2, 256);
-        {
-            // Warp w: TMEM lanes 32*(w%4).., Q columns [64*(w/4), 64*(w/4)+64).
-            const int arow = (warp & 3) * 32 + lane, half_cols = warp >> 2;
-            const uint8_t *mine = qstage + arow * 512;
-            const uint32_t qdst = tmem + ((uint32_t)((warp & 3) * 32) << 16) + TM_Q + half_cols * 64;
+        uint8_t *qstage = smem + L::SM_P;                             // 128 A rows x 256 bytes
+        const int sub = (lane & 1) * 8;
+        const int arow = (warp & 3) * 32 + lane, col_half = warp >> 2;
+        const uint32_t qdst = tmem + ((uint32_t)((warp & 3) * 32) << 16) + TM_Q + col_half * 32;
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
+        for (int round = 0; round < 2; ++round) {
+#pragma unroll
+            for (int j = 0; j < QR; ++j) {
+                const int rr = warp + 8 * j;
+                const int ahi = 32 * (rr >> 4) + (rr & 15);
+                const int p0 = (((lane >> 1) ^ (ahi & 7)) << 4) + sub;
+                *reinterpret_cast<uint2 *>(qstage + ahi * 256 + p0) = make_uint2(hw[j][round][0], hw[j][round][1]);
+                *reinterpret_cast<uint2 *>(qstage + (ahi + 16) * 256 + p0) = make_uint2(hw[j][round][2], hw[j][round][3]);
+            }
+            named_barrier(2, 256);
+            // Warp w: TMEM lanes 32*(w%4).., columns 64*round + [32*(w/4), 32*(w/4)+32).
+            const uint8_t *mine = qstage + arow * 256;
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
                 uint4 u[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                    u[e] = *reinterpret_cast<const uint4 *>(mine + (((half_cols * 16 + 4 * m + e) ^ (lane & 7)) << 4));
-                tmem_st16(qdst + m * 16, *reinterpret_cast<const float(*)[16]>(u));
+                    u[e] = *reinterpret_cast<const uint4 *>(mine + (((col_half * 8 + 4 * m + e) ^ (lane & 7)) << 4));
+                tmem_st16(qdst + round * 64 + m * 16, *reinterpret_cast<const float(*)[16]>(u));
             }
+            if (round == 0) named_barrier(3, 256);    // every warp has read round 0 before it is overwritten
+        }
+        {
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(q_ready);
+            if (threadIdx.x == 128) QV_STAMP(3);
         }
         if ((warp == 2 || warp == 3) && appends) {
             // Append: RMSNorm + rotary of the new keys, fp16 keys / values into
@@ -396,8 +707,6 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 uint8_t *kd = smem + L::SM_KV + s * L::SM_KV_STAGE, *vd = kd + TILE_BYTES;
                 if (j == app_tile && !mbar_wait(app_done, 0, abort_flag)) break;   // new rows written
                 if (j >= STAGES3 && !mbar_wait(k_empty + s, (use - 1) & 1, abort_flag)) break;
-                // Fused decode: stage 2 holds the staged queries until they are in TMEM.
-                if (PRECISE && p.fused && j == 2 && !mbar_wait(q_ready, 0, abort_flag)) break;
                 mbar_expect_tx(k_full + s, TILE_BYTES);
                 for (int c = 0; c < 4; ++c) tma_load_2d(kd + c * BN * 128, &tmK, k_full + s, kv_head * HD + c * 64, y);
                 k_issued = j + 1;
@@ -406,6 +715,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 for (int c = 0; c < 4; ++c) tma_load_2d(vd + c * BN * 128, &tmV, v_full + s, kv_head * HD + c * 64, y);
                 v_issued = j + 1;
             }
+            QV_STAMP(9);
             // Drain: every issued load must land before the CTA may exit.
             const long long t0 = clock64();
             for (int j = max(0, k_issued - STAGES3); j < k_issued; ++j)
@@ -463,6 +773,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 if (j >= 1) ok = issue_pv(j - 1);
             }
             if (ok && ntiles > 0) issue_pv(ntiles - 1);
+            QV_STAMP(10);
             // All MMAs of this thread must finish before TMEM is released.
             mma_commit(mma_done);
             const long long t0 = clock64();
@@ -488,6 +799,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         for (int j = 0; j < ntiles; ++j) {
             const int b = j & 1;
             if (!warp_wait(s_full + b, (j >> 1) & 1, abort_flag)) { ok = false; break; }
+            if (j == 0 && threadIdx.x == 128) QV_STAMP(4);
             tc_fence_after();
             float x[64];
             if (PRECISE) {
@@ -595,8 +907,26 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + b);
         }
-        if (PRECISE) l += __shfl_xor_sync(0xffffffffu, l, 16);
-        if (!PRECISE) {
+        if (threadIdx.x == 128) QV_STAMP(5);
+        if (PRECISE) {
+            // The row's running max and sum, for the epilogue of all warps
+            // (the rotary table is no longer read: every new row is appended).
+            l += __shfl_xor_sync(0xffffffffu, l, 16);
+            if (half == 0) {
+                float *ml_s = reinterpret_cast<float *>(smem + L::SM_ROPE);
+                ml_s[2 * r] = m_use;
+                ml_s[2 * r + 1] = l;
+            }
+            if (valid && half == 0) {
+                if (p.mode == 1) {
+                    if (p.lse) p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * LN2 : -INFINITY;
+                } else {
+                    const size_t slot = ((size_t)kv_head * DECODE_ROWS + r) * MAXS + blockIdx.x;
+                    p.part_ml[slot * 2] = m_use;
+                    p.part_ml[slot * 2 + 1] = l;
+                }
+            }
+        } else {
             // Warpgroup 1 hands its row sums to warpgroup 0, which writes the output.
             float *lx = xch + (ntiles & 1) * 256;     // the exchange buffer no tile still reads
             if (wg == 1) {
@@ -610,27 +940,18 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 ok = false;
             }
         }
-        // Epilogue: the final PV's commit on p_free marks O complete (and every
-        // K/V tile consumed, so the ring is idle).  O leaves through shared
-        // memory: every lane puts its TMEM lane (PRECISE: O_hi in lanes i,
-        // O_lo in lanes 16+i) into a padded staging row, then the warp stores
-        // each output row (the sum of its hi and lo rows) as 512-byte pieces.
-        if (ok && ntiles > 0 && warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag)) {
+        // FAST epilogue: the final PV's commit on p_free marks O complete (and
+        // every K/V tile consumed, so the ring is idle).  O leaves through shared
+        // memory: every lane puts its TMEM lane into a padded staging row, then
+        // the warp stores each output row as 512-byte pieces.
+        if (!PRECISE && ok && ntiles > 0 &&
+            warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag)) {
             tc_fence_after();
-            constexpr int WROWS = PRECISE ? 16 : 32;               // logical rows of this warp
             constexpr int RSTRIDE = HD * 4 + 16;                   // staging row bytes (padded)
             static_assert(4 * 32 * RSTRIDE <= STAGES3 * L::SM_KV_STAGE, "O staging exceeds the K/V ring");
             uint8_t *stage = smem + L::SM_KV + wq * 32 * RSTRIDE;
-            const float inv = p.direct ? (l > 0.f ? 1.f / l : 0.f) : 1.f;
-            if (valid && (!PRECISE || half == 0)) {
-                if (p.direct) {
-                    if (p.lse) p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * 0.6931471805599453f : -INFINITY;
-                } else {
-                    const size_t slot = ((size_t)kv_head * p.splits + blockIdx.x) * DECODE_ROWS + r;
-                    p.part_ml[slot * 2] = m_use;
-                    p.part_ml[slot * 2 + 1] = l;
-                }
-            }
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            if (valid && p.lse) p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * LN2 : -INFINITY;
             uint8_t *myrow = stage + lane * RSTRIDE;
 #pragma unroll 1
             for (int c4 = 0; c4 < HD / 64; ++c4) {                 // 64 columns per TMEM round trip
@@ -647,39 +968,100 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             }
             __syncwarp();
             // The valid logical rows of a CTA are a prefix, so are this warp's.
-            const int row0 = PRECISE ? wq * 16 : wq * 32;
-            const int nvalid = max(0, min(WROWS, (p.mode == 0 ? p.T * GROUP
-                                                              : p.T - (int)(gridDim.y - 1 - blockIdx.y) * QROWS) - row0));
+            const int row0 = wq * 32;
+            const int nvalid = max(0, min(32, p.T - (int)(gridDim.y - 1 - blockIdx.y) * QROWS - row0));
+#pragma unroll 4
+            for (int i = 0; i < nvalid; ++i) {
+                int tt, hh;
+                row_token_head<QROWS>(p, row0 + i, tt, hh);
+                float *dst = p.out + ((size_t)tt * NQ + hh) * HD;
+#pragma unroll
+                for (int part = 0; part < 2; ++part) {
+                    const int col = part * 128 + 4 * lane;
+                    *reinterpret_cast<float4 *>(dst + col) = *reinterpret_cast<const float4 *>(stage + i * RSTRIDE + col * 4);
+                }
+            }
+        }
+    }
+    if (PRECISE) {
+        // ------------------------------------------------ epilogue (all 8 warps)
+        // The final PV's commit on p_free marks O complete (and every K/V tile
+        // consumed, so the ring is idle).  Warps w and w+4 share TMEM lane
+        // quarter w%4 (O_hi of row 16(w%4)+i in lane i, O_lo in lane 16+i) and
+        // take O columns [0,128) (warps 4-7) and [128,256) (warps 0-3): each lane
+        // puts its lane's columns into a padded staging row, then the warp
+        // stores each of its rows, the sum of its hi and lo staging rows, as
+        // 512-byte pieces: decode rows as this split's unnormalised partial,
+        // prefill rows divided by their sum and gated.
+        __syncwarp();                                      // warps 0 and 1: lane 0 is back from its role
+        named_barrier(5, 256);                             // the rows' (max, sum) are in shared memory
+        const bool o_ready = ntiles > 0 &&
+                             warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag);
+        if (o_ready) {
+            tc_fence_after();
+            const int chalf = warp < 4 ? 1 : 0;
+            constexpr int RS = 128 * 4 + 16;                       // staging row bytes (padded)
+            static_assert(8 * 32 * RS <= STAGES3 * L::SM_KV_STAGE, "O staging exceeds the K/V ring");
+            uint8_t *stage = smem + L::SM_KV + warp * 32 * RS;
+            uint8_t *myrow = stage + lane * RS;
+            const uint32_t ocol = t_lane + TM_O + chalf * 128;
+#pragma unroll
+            for (int c4 = 0; c4 < 2; ++c4) {                       // 64 columns per TMEM round trip
+                float o[4][16];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) tmem_ld16(ocol + c4 * 64 + q * 16, o[q]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<float4 *>(myrow + (c4 * 64 + q * 16 + e) * 4) =
+                            make_float4(o[q][e], o[q][e + 1], o[q][e + 2], o[q][e + 3]);
+            }
+            __syncwarp();
+            const float *ml_s = reinterpret_cast<const float *>(smem + L::SM_ROPE);
+            const bool direct = p.mode == 1;                       // prefill: final rows; decode: split partials
+            // The valid logical rows of a CTA are a prefix, so are this warp's.
+            const int row0 = wq * 16;
+            const int nvalid = max(0, min(16, (p.mode == 0 ? p.T * GROUP
+                                                           : p.T - (int)(gridDim.y - 1 - blockIdx.y) * QROWS) - row0));
+            const int col = 4 * lane;
 #pragma unroll 4
             for (int i = 0; i < nvalid; ++i) {
                 const int rr = row0 + i;
                 int tt, hh;
                 row_token_head<QROWS>(p, rr, tt, hh);
-                float *dst = p.direct ? p.out + ((size_t)tt * NQ + hh) * HD
-                                      : p.part_o + (((size_t)kv_head * p.splits + blockIdx.x) * DECODE_ROWS + rr) * HD;
-                const float *gate = p.direct && p.q_gate ? p.q_gate + ((size_t)tt * NQ + hh) * 2 * HD + HD : nullptr;
-#pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    const int col = part * 128 + 4 * lane;
-                    float4 v = *reinterpret_cast<const float4 *>(stage + i * RSTRIDE + col * 4);
-                    if (PRECISE) {
-                        const float4 w = *reinterpret_cast<const float4 *>(stage + (i + 16) * RSTRIDE + col * 4);
-                        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-                    }
-                    if (gate) {
-                        const float4 g = *reinterpret_cast<const float4 *>(gate + col);
+                float4 v = *reinterpret_cast<const float4 *>(stage + i * RS + col * 4);
+                const float4 w = *reinterpret_cast<const float4 *>(stage + (i + 16) * RS + col * 4);
+                v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+                float *dst;
+                if (direct) {
+                    const float lr = ml_s[2 * rr + 1], inv = lr > 0.f ? 1.f / lr : 0.f;
+                    v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
+                    if (p.q_gate) {
+                        const float4 g = *reinterpret_cast<const float4 *>(
+                            p.q_gate + ((size_t)tt * NQ + hh) * 2 * HD + HD + chalf * 128 + col);
                         v.x *= sigmoidf_(g.x); v.y *= sigmoidf_(g.y);
                         v.z *= sigmoidf_(g.z); v.w *= sigmoidf_(g.w);
                     }
-                    *reinterpret_cast<float4 *>(dst + col) = v;
+                    dst = p.out + ((size_t)tt * NQ + hh) * HD;
+                } else {
+                    dst = p.part_o + (((size_t)kv_head * DECODE_ROWS + rr) * p.splits + blockIdx.x) * HD;
                 }
+                *reinterpret_cast<float4 *>(dst + chalf * 128 + col) = v;
             }
+            if (threadIdx.x == 128) QV_STAMP(6);
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, 512);
+    if (threadIdx.x == 0) QV_STAMP(11);
+    // Decode: the split combine of this CTA's share of the KV head's rows
+    // (the K/V ring and the P buffers are idle now; the P region is scratch).
+    if (PRECISE && p.mode == 0)
+        decode_tail(p, kv_head, smem + L::SM_P, reinterpret_cast<float *>(smem + L::SM_KV), cbar, abort_flag);
 }
 
 // ---------------------------------------------------------------- prepare
@@ -725,203 +1107,6 @@ attn_prepare_kernel(const float *q_gate, const float *key, const float *value, c
         kc[o] = __float2half_rn(row[i]);
         vc[o] = __float2half_rn(value[((size_t)t * NKV + kh) * HD + i]);
     }
-}
-
-// ---------------------------------------------------------------- combine
-// Merge the split partials of one (token, head) row: weights from the
-// per-split (max, sum) are formed once in shared memory, then each thread
-// (one output dimension) streams the splits with 8 independent loads in
-// flight.  final_gate 1: gated output; 0: normalised partial + natural-log LSE.
-constexpr int MAX_SPLITS = 64;
-__global__ void __launch_bounds__(256)
-attn_combine_kernel(float *out, float *out_lse, const float *part_o, const float *part_ml,
-                    const float *q_gate, int splits, int final_gate) {
-    const int t = blockIdx.x / NQ, h = blockIdx.x % NQ, d = threadIdx.x;
-    const int g = h / GROUP, r = t * GROUP + h % GROUP;
-    __shared__ float wgt[MAX_SPLITS], red[2], den_s;
-    const size_t slot0 = (size_t)g * splits * DECODE_ROWS + r;     // slot(s) = slot0 + s*DECODE_ROWS
-    grid_dependency_wait();
-    launch_dependents();
-    // Every split's value and (max, sum) are loaded before any is used: one
-    // memory round trip.
-    const float *src = part_o + slot0 * HD + d;
-    float v[MAX_SPLITS];
-#pragma unroll
-    for (int e = 0; e < MAX_SPLITS; ++e) v[e] = e < splits ? src[(size_t)e * DECODE_ROWS * HD] : 0.f;
-    float m = -INFINITY, l = 0.f;
-    if (d < splits) {
-        const float2 ml = *reinterpret_cast<const float2 *>(part_ml + (slot0 + (size_t)d * DECODE_ROWS) * 2);
-        m = ml.x; l = ml.y;
-    }
-    float M = m;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if (d < 64 && (d & 31) == 0) red[d >> 5] = M;
-    __syncthreads();
-    M = fmaxf(red[0], red[1]);
-    const float w = (d < splits && m != -INFINITY) ? exp2f(m - M) : 0.f;
-    if (d < MAX_SPLITS) wgt[d] = w;     // zero for d >= splits
-    float den = w * l;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    __syncthreads();
-    if (d < 64 && (d & 31) == 0) red[d >> 5] = den;
-    __syncthreads();
-    if (d == 0) den_s = red[0] + red[1];
-    __syncthreads();
-    den = den_s;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int e = 0; e < MAX_SPLITS; ++e) acc[e & 3] += wgt[e] * v[e];
-    const float num = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-    const size_t o = ((size_t)t * NQ + h) * HD + d;
-    if (final_gate) {
-        out[o] = (den > 0.f ? num / den : 0.f) * sigmoidf_(q_gate[((size_t)t * NQ + h) * 2 * HD + HD + d]);
-    } else {
-        out[o] = den > 0.f ? num / den : 0.f;
-        if (d == 0) out_lse[(size_t)t * NQ + h] = den > 0.f ? (M + log2f(den)) * 0.6931471805599453f : -INFINITY;
-    }
-}
-
-// ---------------------------------------------------------------- fused shard exchange
-// Multi-GPU verify: one CTA per (token, head) row combines this shard's split
-// partials of the row, stores the normalised partial and its LSE into slot
-// [rank] of every other rank's receive buffer (peer memory over NVLink), then
-// reads the other ranks' partials of the row from its own buffer and merges
-// them (O = sum_g exp(lse_g - LSE) O_g, times sigmoid(gate)).
-//
-// Every value travels as a 64-bit word {value bits, tag}: the reader spins on
-// each of its words until the tag of this call appears, so no fence or
-// separate flag write is needed, and it zeroes each word after reading it.
-// Receive buffer of each rank: [2 slots][world][EX_ROWS][EX_WORDS] words (256
-// O, lse, padding).  `seq` counts the calls on these buffers (the same on
-// every rank, +1 per call): its parity picks the slot and its low 24 bits are
-// in the tag.  A rank writes into a slot again two calls later, after it has
-// received this rank's partials of the call in between, and that call started
-// only after this one (and its zeroing) completed.  A word that arrives after
-// its reader gave up (a timeout) stays behind unread, but it carries the tag
-// of its own call and the next call on that slot waits for a different tag,
-// so it is never taken for new data.  The CTAs of one launch hold no shared
-// memory to speak of, so all of them are resident at once and every awaited
-// word has a running writer on its rank.
-constexpr int EX_ROWS = MAX_DECODE_T * NQ;       // rows of the largest decode batch
-constexpr int EX_WORDS = 264;                    // words per row: 256 O + lse, padded to 64 bytes
-constexpr int EX_MAX_WORLD = 8;
-__host__ __device__ constexpr uint32_t ex_tag(int seq) {   // high half of a filled word; never 0
-    return 0x51000000u | ((uint32_t)seq & 0x00FFFFFFu);
-}
-__host__ __device__ constexpr size_t ex_bytes(int world) {
-    return (size_t)2 * world * EX_ROWS * EX_WORDS * sizeof(uint64_t);
-}
-
-__global__ void __launch_bounds__(256)
-attn_exchange_kernel(float *out, const float *part_o, const float *part_ml, int splits, const float *q_gate,
-                     const uint64_t *peers, int world, int rank, int seq) {
-    const int d = threadIdx.x, row = blockIdx.x, slot = seq & 1;
-    const uint32_t tag32 = ex_tag(seq);
-    const int t = row / NQ, h = row % NQ, g = h / GROUP, r = t * GROUP + h % GROUP;
-    __shared__ float wgt[MAX_SPLITS], red[2], den_s, lse_s[EX_MAX_WORLD];
-    grid_dependency_wait();
-    launch_dependents();
-    // ---- this shard's partial of the row (split combine, one round trip)
-    const size_t slot0 = (size_t)g * splits * DECODE_ROWS + r;
-    const float *src = part_o + slot0 * HD + d;
-    float v[MAX_SPLITS];
-#pragma unroll
-    for (int e = 0; e < MAX_SPLITS; ++e) v[e] = e < splits ? src[(size_t)e * DECODE_ROWS * HD] : 0.f;
-    float m = -INFINITY, l = 0.f;
-    if (d < splits) {
-        const float2 ml = *reinterpret_cast<const float2 *>(part_ml + (slot0 + (size_t)d * DECODE_ROWS) * 2);
-        m = ml.x; l = ml.y;
-    }
-    float M = m;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if (d < 64 && (d & 31) == 0) red[d >> 5] = M;
-    __syncthreads();
-    M = fmaxf(red[0], red[1]);
-    const float w = (d < splits && m != -INFINITY) ? exp2f(m - M) : 0.f;
-    if (d < MAX_SPLITS) wgt[d] = w;
-    float den = w * l;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    __syncthreads();
-    if (d < 64 && (d & 31) == 0) red[d >> 5] = den;
-    __syncthreads();
-    if (d == 0) den_s = red[0] + red[1];
-    __syncthreads();
-    den = den_s;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int e = 0; e < MAX_SPLITS; ++e) acc[e & 3] += wgt[e] * v[e];
-    const float o = den > 0.f ? ((acc[0] + acc[1]) + (acc[2] + acc[3])) / den : 0.f;
-    const float lse = den > 0.f ? (M + log2f(den)) * 0.6931471805599453f : -INFINITY;
-
-    // ---- push it to every other rank
-    const uint64_t tag = (uint64_t)tag32 << 32;
-    for (int q = 0; q < world; ++q) {
-        if (q == rank) continue;
-        uint64_t *dst = reinterpret_cast<uint64_t *>(peers[q]) +
-                        (((size_t)slot * world + rank) * EX_ROWS + row) * EX_WORDS;
-        st_word_sys(dst + d, tag | __float_as_uint(o));
-        if (d == 0) st_word_sys(dst + HD, tag | __float_as_uint(lse));
-    }
-
-    // ---- receive the other ranks' partials of the row and merge.  The words of
-    //      all peers are read at once, so their latencies overlap; a word whose
-    //      flag is not there yet is re-read until it is (bounded).
-    uint64_t *own = reinterpret_cast<uint64_t *>(peers[rank]);
-    const long long t0 = clock64();
-    bool ok = true;
-    auto finish = [&](uint64_t *word, uint64_t x, float fallback) {
-        while ((uint32_t)(x >> 32) != tag32) {
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok = false; return fallback; }
-            x = ld_word_sys(word);
-        }
-        *word = 0;
-        return __uint_as_float((uint32_t)x);
-    };
-    auto word_of = [&](int q, int col) {
-        return own + (((size_t)slot * world + q) * EX_ROWS + row) * EX_WORDS + col;
-    };
-    uint64_t first[EX_MAX_WORLD], lse_first = 0;
-    const bool lse_reader = d < world && d != rank;
-    if (lse_reader) lse_first = ld_word_sys(word_of(d, HD));
-#pragma unroll
-    for (int q = 0; q < EX_MAX_WORLD; ++q)
-        first[q] = (q < world && q != rank) ? ld_word_sys(word_of(q, d)) : 0;
-    if (d < world) {
-        float x = lse;
-        if (lse_reader) x = finish(word_of(d, HD), lse_first, x);
-        lse_s[d] = x;
-    }
-    float val[EX_MAX_WORLD];
-#pragma unroll
-    for (int q = 0; q < EX_MAX_WORLD; ++q) {
-        val[q] = 0.f;
-        if (q < world) {
-            if (q == rank) val[q] = o;
-            else val[q] = finish(word_of(q, d), first[q], 0.f);
-        }
-    }
-    const int all_ok = __syncthreads_and(ok);
-    float res = 0.f;
-    if (all_ok) {
-        float Mx = -INFINITY;
-        for (int q = 0; q < world; ++q) Mx = fmaxf(Mx, lse_s[q]);
-        float num = 0.f, dsum = 0.f;
-        if (Mx != -INFINITY) {
-#pragma unroll
-            for (int q = 0; q < EX_MAX_WORLD; ++q) {
-                if (q >= world || lse_s[q] == -INFINITY) continue;
-                const float wq = expf(lse_s[q] - Mx);
-                dsum += wq;
-                num += wq * val[q];
-            }
-        }
-        res = dsum > 0.f ? num / dsum : 0.f;
-    }
-    out[((size_t)t * NQ + h) * HD + d] = res * sigmoidf_(q_gate[((size_t)t * NQ + h) * 2 * HD + HD + d]);
 }
 
 // Merge per-GPU shard partials (normalised O, natural-log LSE) into the gated
@@ -996,12 +1181,24 @@ void configure() {
 }
 
 struct Split { int tiles, splits; };
-// Split-KV plan: about 37 CTAs per KV head (148 SMs / 4 heads), whole tiles
-// per split.  The plan depends only on the cache length.
+// CTAs per KV head of a decode launch: a quarter of the SMs (37 on B200), so
+// that the four heads fill one wave with one CTA per SM and the CTAs of a
+// head, which meet at the tail barrier, are all resident at once.  Without a
+// device (host-side size queries) the B200 figure is used.
+int decode_ctas_per_head() {
+    int dev = -1, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        sms = 148;
+    }
+    return std::max(1, std::min(37, sms / NKV));
+}
+// Split-KV plan: whole tiles per split, at most decode_ctas_per_head() splits.
 Split decode_split(int kv_rows) {
-    const int total = (kv_rows + BN - 1) / BN;
-    const int per = (total + 36) / 37;
-    static_assert(37 <= MAX_SPLITS, "combine kernel handles up to MAX_SPLITS splits");
+    const int total = std::max(1, (kv_rows + BN - 1) / BN);
+    const int ctas = decode_ctas_per_head();
+    const int per = (total + ctas - 1) / ctas;
+    static_assert(37 <= MAXS, "the tail combine handles up to MAXS splits");
     return {per, (total + per - 1) / per};
 }
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -1014,36 +1211,44 @@ void launch_fa(const CUtensorMap &mk, const CUtensorMap &mv, const FaParams &p, 
     if (e != cudaSuccess) throw std::runtime_error(std::string("attention kernel launch: ") + cudaGetErrorString(e));
 }
 
-// Split partials of a decode / verify launch inside the workspace.
-struct DecodeParts { float *o, *ml; };
+// Decode workspace: the tail barrier's words (256 bytes: one 64-bit word per
+// KV head, generation : arrivals; the arrivals must be zero before the first
+// launch on the workspace and every launch leaves them zero), then the split
+// partials.
+constexpr size_t SYNC_BYTES = 256;
+struct DecodeParts { unsigned long long *sync; float *o, *ml; };
 size_t decode_parts_bytes(const Split &sp) {
-    return align256((size_t)NKV * sp.splits * DECODE_ROWS * HD * sizeof(float)) +
-           align256((size_t)NKV * sp.splits * DECODE_ROWS * 2 * sizeof(float));
+    return SYNC_BYTES + align256((size_t)NKV * sp.splits * DECODE_ROWS * HD * sizeof(float)) +
+           align256((size_t)NKV * DECODE_ROWS * MAXS * 2 * sizeof(float));
 }
 DecodeParts decode_parts(void *ws, const Split &sp) {
-    float *o = static_cast<float *>(ws);
-    float *ml = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) +
-                                          align256((size_t)NKV * sp.splits * DECODE_ROWS * HD * sizeof(float)));
-    return {o, ml};
+    uint8_t *w = static_cast<uint8_t *>(ws);
+    float *o = reinterpret_cast<float *>(w + SYNC_BYTES);
+    float *ml = reinterpret_cast<float *>(w + SYNC_BYTES + align256((size_t)NKV * sp.splits * DECODE_ROWS * HD * sizeof(float)));
+    return {reinterpret_cast<unsigned long long *>(w), o, ml};
 }
 
-// Split-KV decode / verify with the prepare step folded in: one launch
-// normalises and rotates the queries, appends the new keys / values (when
-// `append`) and writes the split partials of every (token, head) row.
-Split launch_decode(__half *kc, __half *vc, const float *q_gate, const float *key, const float *value,
-                    const float *qn, const float *kn, int T, int position, int kv_begin, int kv_rows, bool append,
-                    float eps, const DecodeParts &parts, cudaStream_t st) {
+// Split-KV decode / verify, one launch: the CTAs normalise and rotate the
+// queries, append the new keys / values (when `append`), attend over their
+// split, and at the tail combine the splits and write the rows as `tail`
+// says (out = gated output, or shard partial with lse, or the peer exchange).
+void launch_decode(float *out, float *lse, __half *kc, __half *vc, const float *q_gate, const float *key,
+                   const float *value, const float *qn, const float *kn, int T, int position, int kv_begin,
+                   int kv_rows, bool append, float eps, void *ws, size_t ws_bytes, DecodeTail tail,
+                   const uint64_t *peers, int world, int rank, int seq, cudaStream_t st) {
     configure();
-    const CUtensorMap mk = cache_map(kc, kv_rows), mv = cache_map(vc, kv_rows);
     const Split sp = decode_split(kv_rows);
+    if (ws_bytes < decode_parts_bytes(sp)) throw std::invalid_argument("attention workspace too small");
+    const DecodeParts parts = decode_parts(ws, sp);
+    const CUtensorMap mk = cache_map(kc, kv_rows), mv = cache_map(vc, kv_rows);
     FaParams p{};
-    p.q_gate = q_gate; p.T = T; p.position = position; p.kv_begin = kv_begin; p.kv_rows = kv_rows;
-    p.mode = 0; p.split_tiles = sp.tiles; p.splits = sp.splits; p.direct = 0;
-    p.part_o = parts.o; p.part_ml = parts.ml;
+    p.q_gate = q_gate; p.out = out; p.lse = lse; p.T = T; p.position = position; p.kv_begin = kv_begin;
+    p.kv_rows = kv_rows; p.mode = 0; p.split_tiles = sp.tiles; p.splits = sp.splits;
+    p.part_o = parts.o; p.part_ml = parts.ml; p.sync = parts.sync;
+    p.tail = tail; p.peers = peers; p.world = world; p.rank = rank; p.seq = seq;
     p.fused = 1; p.key = key; p.value = value; p.qn = qn; p.kn = kn; p.kc = kc; p.vc = vc;
     p.append_row0 = append ? position - kv_begin : -1; p.eps = eps;
     launch_fa<true>(mk, mv, p, dim3(sp.splits, NKV), st);
-    return sp;
 }
 }  // namespace
 
@@ -1058,8 +1263,8 @@ int attention_max_shard_batch() { return MAX_DECODE_T; }
 // [kv_begin, kv_begin + kv_rows).  New rows are appended at local row
 // position - kv_begin when append is true.  Writes either the final gated
 // output (shard_lse == nullptr) or a normalised partial + LSE (shard mode).
-// Decode / verify batches (T <= 10) use the split-KV regime (one fused
-// launch + the split combine); longer blocks use the prefill regime with 64
+// Decode / verify batches (T <= 10) use the split-KV regime (one launch, the
+// split combine in its tail); longer blocks use the prefill regime with 64
 // query rows per CTA after a prepare launch; both are PRECISE.
 void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const float *q_gate,
                    const float *key, const float *value, const float *qn, const float *kn, int T,
@@ -1067,12 +1272,8 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
                    size_t ws_bytes, cudaStream_t st) {
     if (ws_bytes < attention_workspace_bytes(T, kv_rows)) throw std::invalid_argument("attention workspace too small");
     if (decode_regime(T)) {
-        const DecodeParts parts = decode_parts(ws, decode_split(kv_rows));
-        const Split sp = launch_decode(kc, vc, q_gate, key, value, qn, kn, T, position, kv_begin, kv_rows, append,
-                                       eps, parts, st);
-        const cudaError_t e = launch_chained(attn_combine_kernel, dim3(T * NQ), dim3(256), 0, st, out, shard_lse,
-                                             parts.o, parts.ml, q_gate, sp.splits, shard_lse ? 0 : 1);
-        if (e != cudaSuccess) throw std::runtime_error(std::string("attention combine: ") + cudaGetErrorString(e));
+        launch_decode(out, shard_lse, kc, vc, q_gate, key, value, qn, kn, T, position, kv_begin, kv_rows, append, eps,
+                      ws, ws_bytes, shard_lse ? TAIL_SHARD : TAIL_GATED, nullptr, 1, 0, 0, st);
         return;
     }
     if (shard_lse) throw std::invalid_argument("shard partials are limited to decode batches");
@@ -1087,7 +1288,7 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
     FaParams p{};
     p.q = qw; p.q_lo = qw_lo; p.q_gate = q_gate; p.T = T; p.position = position;
     p.kv_begin = kv_begin; p.kv_rows = kv_rows;
-    p.mode = 1; p.direct = 1; p.out = out; p.splits = 1;
+    p.mode = 1; p.out = out; p.splits = 1;
     constexpr int R = FaLayout<true>::QROWS;
     launch_fa<true>(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
 }
@@ -1095,7 +1296,8 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
 size_t attention_exchange_bytes(int world) { return ex_bytes(world); }
 int attention_exchange_max_world() { return EX_MAX_WORLD; }
 
-// Shard attention + fused all-to-all exchange + merge (see attn_exchange_kernel).
+// Shard attention + all-to-all exchange + merge, one launch (the exchange is
+// the decode kernel's tail, see exchange_rows).
 void attention_shard_exchange(float *out, __half *kc, __half *vc, const float *q_gate, const float *key,
                               const float *value, const float *qn, const float *kn, int T, int position,
                               int kv_begin, int kv_rows, bool append, float eps, const uint64_t *peers,
@@ -1104,12 +1306,8 @@ void attention_shard_exchange(float *out, __half *kc, __half *vc, const float *q
     if (world < 1 || world > EX_MAX_WORLD || rank < 0 || rank >= world || seq < 0)
         throw std::invalid_argument("invalid exchange group");
     if (ws_bytes < attention_workspace_bytes(T, kv_rows)) throw std::invalid_argument("attention workspace too small");
-    const DecodeParts parts = decode_parts(ws, decode_split(kv_rows));
-    const Split sp = launch_decode(kc, vc, q_gate, key, value, qn, kn, T, position, kv_begin, kv_rows, append, eps,
-                                   parts, st);
-    const cudaError_t e = launch_chained(attn_exchange_kernel, dim3(T * NQ), dim3(256), 0, st, out, parts.o, parts.ml,
-                                         sp.splits, q_gate, peers, world, rank, seq);
-    if (e != cudaSuccess) throw std::runtime_error(std::string("attention exchange: ") + cudaGetErrorString(e));
+    launch_decode(out, nullptr, kc, vc, q_gate, key, value, qn, kn, T, position, kv_begin, kv_rows, append, eps, ws,
+                  ws_bytes, TAIL_EXCHANGE, peers, world, rank, seq, st);
 }
 
 void attention_merge(float *out, const float *parts, const float *lses, int shards, int T,
@@ -1129,7 +1327,7 @@ void prefill_core(float *out, float *lse, const __half *q, const __half *kc, con
     const CUtensorMap mk = cache_map(kc, kv_rows), mv = cache_map(vc, kv_rows);
     FaParams p{};
     p.q = q; p.T = T; p.position = position; p.kv_begin = 0; p.kv_rows = kv_rows;
-    p.mode = 1; p.direct = 1; p.out = out; p.lse = lse; p.splits = 1;
+    p.mode = 1; p.out = out; p.lse = lse; p.splits = 1;
     constexpr int R = FaLayout<false>::QROWS;
     launch_fa<false>(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
     check_launch("prefill attention");

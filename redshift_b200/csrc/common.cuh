@@ -25,6 +25,24 @@ constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;   // ~2 s at 1.9 GHz
 
 __device__ __forceinline__ void raise_status(int code) { atomicCAS(&g_status, 0, code); }
 
+// Phase timestamps for latency studies.  Compiled in only when the library is
+// built with QV_TIMELINE defined (never in the product build): the calling
+// thread stores %globaltimer into slot `i` of its CTA's row of g_timeline
+// ([QV_TIMELINE_CTAS][QV_TIMELINE_SLOTS], read back by qv_timeline_read).
+#ifdef QV_TIMELINE
+constexpr int QV_TIMELINE_CTAS = 1024, QV_TIMELINE_SLOTS = 16;
+extern __device__ unsigned long long g_timeline[QV_TIMELINE_CTAS * QV_TIMELINE_SLOTS];
+__device__ __forceinline__ void qv_stamp(int i) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (cta < (unsigned)QV_TIMELINE_CTAS) g_timeline[cta * QV_TIMELINE_SLOTS + i] = t;
+}
+#define QV_STAMP(i) qv_stamp(i)
+#else
+#define QV_STAMP(i) ((void)0)
+#endif
+
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -162,6 +180,20 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_
 }
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
+}
+// L2 prefetch hint: it moves nothing into the CTA and leaves no copy that a
+// later write could make stale (L2 is the device's point of coherence), so it
+// may be issued before the grid-dependency wait, while the previous kernel
+// still runs.
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" :: "l"(p));
+}
+
+// Device-scope acquire load (for a word written by other CTAs of a grid).
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // ---------------------------------------------------------------- tcgen05

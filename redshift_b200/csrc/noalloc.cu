@@ -21,7 +21,9 @@
 namespace {
 
 // Fixed scratch: large enough for every decode/verify call of up to 8 tokens
-// at any context up to 139,264 (the largest needs 9,775,104 bytes).
+// at any context up to 139,264 (the largest needs 9,775,360 bytes).  It is
+// zero at load; its first 256 bytes are the attention launch's barrier
+// counters, which must start at zero and which every call leaves at zero.
 constexpr size_t kScratchBytes = 10u << 20;   // 10 MiB per GPU
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 

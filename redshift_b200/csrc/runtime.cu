@@ -48,7 +48,7 @@ size_t checked_bytes(size_t count, size_t elem) {
 // Device allocation owned for the duration of one synchronous call.
 class DeviceBuffer {
   public:
-    explicit DeviceBuffer(size_t bytes) {
+    explicit DeviceBuffer(size_t bytes) : bytes_(bytes) {
         if (bytes) cuda_ok(cudaMalloc(&ptr_, bytes), "device allocation");
     }
     ~DeviceBuffer() { if (ptr_) cudaFree(ptr_); }
@@ -58,11 +58,15 @@ class DeviceBuffer {
     void upload(const void *src, size_t bytes, size_t offset = 0) {
         if (bytes) cuda_ok(cudaMemcpy(static_cast<char *>(ptr_) + offset, src, bytes, cudaMemcpyHostToDevice), "upload");
     }
+    void zero() {
+        if (ptr_) cuda_ok(cudaMemset(ptr_, 0, bytes_), "workspace clear");
+    }
     void download(void *dst, size_t bytes, size_t offset = 0) const {
         if (bytes) cuda_ok(cudaMemcpy(dst, static_cast<const char *>(ptr_) + offset, bytes, cudaMemcpyDeviceToHost), "download");
     }
   private:
     void *ptr_ = nullptr;
+    size_t bytes_ = 0;
 };
 
 // Wait for the device and surface both CUDA errors and kernel status codes.
@@ -104,6 +108,7 @@ void attention_host(float *out, void *key_cache, void *value_cache, const float 
     kn.upload(k_norm, kHeadDim * sizeof(float));
     const size_t ws_bytes = qv::attention_workspace_bytes(batch, n);
     DeviceBuffer ws(ws_bytes);
+    ws.zero();                          // the decode tail's barrier words start at zero
     qv::attention_run(o.get<float>(), nullptr, kc.get<__half>(), vc.get<__half>(), qg.get<float>(),
                       k.get<float>(), v.get<float>(), qn.get<float>(), kn.get<float>(), batch, position,
                       0, n, true, eps, ws.get(), ws_bytes, nullptr);

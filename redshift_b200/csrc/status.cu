@@ -22,4 +22,21 @@ int read_and_clear_status() {
     return value;
 }
 
+#ifdef QV_TIMELINE
+__device__ unsigned long long g_timeline[QV_TIMELINE_CTAS * QV_TIMELINE_SLOTS];
+#endif
+
 }  // namespace qv
+
+#ifdef QV_TIMELINE
+// Latency-study builds only: copy the phase timestamps of the last launches
+// ([1024 CTAs][16 slots] of %globaltimer nanoseconds) to the host and clear them.
+extern "C" int qv_timeline_read(unsigned long long *dst) {
+    const size_t bytes = sizeof(qv::g_timeline);
+    void *addr = nullptr;
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpyFromSymbol(dst, qv::g_timeline, bytes) != cudaSuccess ||
+        cudaGetSymbolAddress(&addr, qv::g_timeline) != cudaSuccess || cudaMemset(addr, 0, bytes) != cudaSuccess)
+        return -1;
+    return 0;
+}
+#endif

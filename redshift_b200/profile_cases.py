@@ -38,7 +38,7 @@ def make_case(hot, case, size):
         val = torch.randn((T, HKV, HD), generator=g, **f32)
         ones = torch.ones(HD, **f32)
         out = torch.empty((T, H, HD), **f32)
-        ws = torch.empty(hot.lib.qv_attention_workspace(T, ctx - T), dtype=torch.uint8, device=dev)
+        ws = torch.zeros(hot.lib.qv_attention_workspace(T, ctx - T), dtype=torch.uint8, device=dev)
         return lambda: hot.attention(out, kc, vc, qg, key, val, ones, ones, T, ctx - T, workspace=ws)
     if case == 'decode_exchange':
         # one rank of the fused peer exchange, exchanging with itself (world = 1)
@@ -50,7 +50,7 @@ def make_case(hot, case, size):
         val = torch.randn((T, HKV, HD), generator=g, **f32)
         ones = torch.ones(HD, **f32)
         out = torch.empty((T, H, HD), **f32)
-        ws = torch.empty(hot.lib.qv_attention_shard_workspace(T, ctx - T), dtype=torch.uint8, device=dev)
+        ws = torch.zeros(hot.lib.qv_attention_shard_workspace(T, ctx - T), dtype=torch.uint8, device=dev)
         buf = torch.zeros(hot.lib.qv_attention_exchange_bytes(1) // 4, dtype=torch.float32, device=dev)
         peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
         state = {'seq': 0}

@@ -121,10 +121,11 @@ class HotPath:
         return ct.c_void_p(t.data_ptr()) if t is not None else None
 
     def workspace(self, nbytes, device):
-        """A cached device workspace of at least ``nbytes`` bytes."""
+        """A cached device workspace of at least ``nbytes`` bytes, zero-filled when it is made (the
+        attention workspace's barrier words must start at zero; the calls keep them so)."""
         import torch
         if self._workspace is None or self._workspace.numel() < nbytes or self._workspace.device != device:
-            self._workspace = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+            self._workspace = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         return self._workspace
 
     # -- attention --------------------------------------------------------

@@ -39,7 +39,7 @@ def _run_pair(lib, case):
             rc = lib.qv_attention_noalloc(ct.c_void_p(out.data_ptr()), ct.c_void_p(kc.data_ptr()),
                                           ct.c_void_p(vc.data_ptr()), *ptrs, batch, position, 1e-6, stream)
         else:
-            ws = torch.empty(lib.qv_attention_workspace(batch, position), dtype=torch.uint8, device=dev)
+            ws = torch.zeros(lib.qv_attention_workspace(batch, position), dtype=torch.uint8, device=dev)
             rc = lib.qv_attention(ct.c_void_p(out.data_ptr()), ct.c_void_p(kc.data_ptr()),
                                   ct.c_void_p(vc.data_ptr()), *ptrs, batch, position, 1e-6,
                                   ct.c_void_p(ws.data_ptr()), ws.numel(), stream)
