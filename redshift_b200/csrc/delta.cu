@@ -48,11 +48,12 @@ __host__ __device__ constexpr size_t delta_trace_floats(int C, int Hv) { return 
 // Grid: CPH CTAs per value head (a cluster); every CTA must own an SM, since
 // an SM holding two CTAs would double the time of its whole cluster.
 // Thread layout: every thread filters one conv channel; the token loop runs
-// on the first 4 * rows threads, 8 per PAIR of state rows and D/8 columns of
-// each (columns 32i + 4j + e), so every k/q value read from shared memory
-// serves two rows (the loop is bound by shared-memory bandwidth) and the four
-// dot products of a token (S_a.k, S_b.k, S_a.q, S_b.q, all against the state
-// before the token's update) reduce together in 4 shuffles.  Per chunk of
+// TPP threads per PAIR of state rows (16 for D = 128: every thread of the
+// CTA; 8 for D = 32), each holding D/TPP columns of both rows (columns
+// 4 TPP i + 4j + e), so every k/q value read from shared memory serves two
+// rows, and the four dot products of a token (S_a.k, S_b.k, S_a.q, S_b.q,
+// all against the state before the token's update) reduce together in one
+// transposing butterfly (5 shuffles over 16 lanes, 4 over 8).  Per chunk of
 // <= 8 tokens:
 //  * the chunk's inputs are loaded one chunk ahead (chunk 0 with the
 //    prologue), so their latency overlaps the previous chunk's scan;
@@ -68,15 +69,20 @@ __host__ __device__ constexpr size_t delta_trace_floats(int C, int Hv) { return 
 // second wave; clusters of 2 always fit (one CTA per SM, 96 SMs).
 template <int D, int CPH> struct DeltaShape {
     static constexpr int MAXR = (D + CPH - 1) / CPH;              // most rows of a rank
-    static constexpr int NT = ((MAXR * 8 + 31) / 32) * 32;         // threads per CTA
+    static constexpr int TPP = D >= 128 ? 16 : 8;                  // token-loop threads per pair of rows
+    static constexpr int LOOP = (MAXR + 1) / 2 * TPP;              // token-loop threads
+    static constexpr int NEED = LOOP > CHUNK * MAXR ? (LOOP > 2 * D + MAXR ? LOOP : 2 * D + MAXR)
+                                                    : (CHUNK * MAXR > 2 * D + MAXR ? CHUNK * MAXR : 2 * D + MAXR);
+    static constexpr int NT = ((NEED > 8 * MAXR ? NEED : 8 * MAXR) + 31) / 32 * 32;   // threads per CTA
 };
 
 template <int D, int CPH, bool CORE, bool RECORD = false>
 __global__ void __cluster_dims__(CPH, 1, 1) __launch_bounds__(DeltaShape<D, CPH>::NT)
 delta_kernel(const DeltaArgs a) {
     static_assert(!(CORE && RECORD), "only the layer mode records a verify");
-    constexpr int MAXR = DeltaShape<D, CPH>::MAXR, NT = DeltaShape<D, CPH>::NT;
-    constexpr int NV4 = D / 32, COLS = D / 8, NW = NT / 32;
+    constexpr int MAXR = DeltaShape<D, CPH>::MAXR, NT = DeltaShape<D, CPH>::NT, TPP = DeltaShape<D, CPH>::TPP;
+    constexpr int COLS = D / TPP, NV4 = COLS / 4, CSTRIDE = 4 * TPP, NW = NT / 32;
+    static_assert(NV4 >= 1 && COLS % 4 == 0, "a thread holds whole float4 groups of its rows");
     static_assert(2 * D + MAXR <= NT, "one conv channel per thread");
     static_assert(CHUNK * MAXR <= NT, "one output per thread per chunk");
     cg::cluster_group cluster = cg::this_cluster();
@@ -85,11 +91,10 @@ delta_kernel(const DeltaArgs a) {
     const int Hk = a.Hk, Hv = a.Hv, kh = h % Hk;
     const int C = (2 * Hk + Hv) * D;
     const int row0 = rank * D / CPH, rows = (rank + 1) * D / CPH - row0;   // this CTA's head rows
-    // token loop: the first 4 * rows threads, 8 per PAIR of state rows (rows
-    // ra, rb), D/8 columns of each; every k/q value read from shared memory
-    // serves both rows
-    const int j = tid & 7, ra = 2 * (tid >> 3), rb = ra + 1;
-    const bool has_a = ra < rows, has_b = rb < rows, scans = tid < 4 * MAXR;
+    // token loop: TPP threads per PAIR of state rows (rows ra, rb), D/TPP
+    // columns of each; every k/q value read from shared memory serves both rows
+    const int j = tid % TPP, ra = 2 * (tid / TPP), rb = ra + 1;
+    const bool has_a = ra < rows, has_b = rb < rows, scans = tid < DeltaShape<D, CPH>::LOOP;
 
     __shared__ __align__(16) float Fq[CHUNK][D], Fk[CHUNK][D], Fv[CHUNK][MAXR];
     __shared__ __align__(16) float O[CHUNK][MAXR];
@@ -99,6 +104,35 @@ delta_kernel(const DeltaArgs a) {
     __shared__ __align__(8) uint64_t osum_bar[2];
     __shared__ bool norm_ok;
 
+    if (tid == 0) QV_STAMP(0);
+    // Conv channel of this thread: e < D -> q, e < 2D -> k, e < 2D + rows -> v row.
+    const int e = tid;
+    int c = -1;
+    if (e < D) c = kh * D + e;
+    else if (e < 2 * D) c = (Hk + kh) * D + (e - D);
+    else if (e < 2 * D + rows) c = (2 * Hk + h) * D + row0 + (e - 2 * D);
+#ifndef QV_DELTA_PREFETCH
+#define QV_DELTA_PREFETCH 1
+#endif
+    if (!CORE && QV_DELTA_PREFETCH) {
+        // L2 prefetch hints, issued before the dependency wait so that their
+        // HBM latency overlaps the previous kernel: this CTA's state block
+        // (rows row0.. of head h, contiguous), and per warp the lines of its
+        // channels' raw inputs, history and conv taps, and of its outputs' gates.
+        const float *sblk = a.state + ((size_t)h * D + row0) * D;
+        for (int i = tid; i < rows * D / 32; i += NT) prefetch_l2(sblk + 32 * i);
+        if (c >= 0 && lane == 0) {
+            for (int t = 0; t < a.T && t < CHUNK; ++t) prefetch_l2(a.qkv + (size_t)t * C + c);
+            for (int r = 0; r < 3; ++r) prefetch_l2(a.history + (size_t)r * C + c);
+        }
+        if (c >= 0 && lane < 4) prefetch_l2(a.conv + (size_t)(c + 7 * lane) * 4);   // channels c0 + 8 lane..
+        if (lane == 0 && tid < CHUNK * rows && tid / rows < a.T)
+            prefetch_l2(a.gate + ((size_t)(tid / rows) * Hv + h) * D + row0 + tid % rows);
+        if (tid < a.T && tid < CHUNK) {
+            prefetch_l2(a.alpha + (size_t)tid * Hv + h);
+            prefetch_l2(a.beta + (size_t)tid * Hv + h);
+        }
+    }
     if (!CORE && tid == 0) {
         // each rank's CHUNK token-warps arrive once per chunk
         mbar_init(&osum_bar[0], CPH * CHUNK);
@@ -108,32 +142,12 @@ delta_kernel(const DeltaArgs a) {
     // Peers arrive on osum_bar only after it is initialised everywhere (this
     // needs no memory written by another kernel, so it overlaps the previous one).
     if (!CORE && CPH > 1) cluster.sync();
+    if (tid == 0) QV_STAMP(1);
     // State, history and inputs may have been written by the previous kernel.
     grid_dependency_wait();
-    if (tid == 0) launch_dependents();
+    if (tid == 0) { launch_dependents(); QV_STAMP(2); }
 
     // ---- loads that do not depend on the chunk
-    float Sa[COLS], Sb[COLS];
-    float *srow_a = a.state + ((size_t)h * D + row0 + (has_a ? ra : 0)) * D;
-    float *srow_b = a.state + ((size_t)h * D + row0 + (has_b ? rb : 0)) * D;
-#pragma unroll
-    for (int i = 0; i < NV4; ++i) {
-        float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
-        if (has_a) va = *reinterpret_cast<const float4 *>(srow_a + 32 * i + 4 * j);
-        if (has_b) vb = *reinterpret_cast<const float4 *>(srow_b + 32 * i + 4 * j);
-        Sa[4 * i] = va.x; Sa[4 * i + 1] = va.y; Sa[4 * i + 2] = va.z; Sa[4 * i + 3] = va.w;
-        Sb[4 * i] = vb.x; Sb[4 * i + 1] = vb.y; Sb[4 * i + 2] = vb.z; Sb[4 * i + 3] = vb.w;
-        if (RECORD && has_a)
-            *reinterpret_cast<float4 *>(a.saved_state + (srow_a - a.state) + 32 * i + 4 * j) = va;
-        if (RECORD && has_b)
-            *reinterpret_cast<float4 *>(a.saved_state + (srow_b - a.state) + 32 * i + 4 * j) = vb;
-    }
-    // Conv channel of this thread: e < D -> q, e < 2D -> k, e < 2D + rows -> v row.
-    const int e = tid;
-    int c = -1;
-    if (e < D) c = kh * D + e;
-    else if (e < 2 * D) c = (Hk + kh) * D + (e - D);
-    else if (e < 2 * D + rows) c = (2 * Hk + h) * D + row0 + (e - 2 * D);
     float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f, h0 = 0.f, h1 = 0.f, h2 = 0.f;
     if (!CORE && c >= 0) {
         const float4 w = *reinterpret_cast<const float4 *>(a.conv + (size_t)c * 4);
@@ -175,6 +189,23 @@ delta_kernel(const DeltaArgs a) {
         gz_n = (!CORE && has_out && out_t < m) ? a.gate[((size_t)(c0 + out_t) * Hv + h) * D + row0 + out_i] : 0.f;
     };
     load_chunk(0);
+    // The state is first needed in the token loop: its loads go out after the
+    // inputs of the conv, which is needed first.
+    float2 Sa[COLS / 2], Sb[COLS / 2];       // column pairs (4i, 4i+1), (4i+2, 4i+3) of float4 group i
+    float *srow_a = a.state + ((size_t)h * D + row0 + (has_a ? ra : 0)) * D;
+    float *srow_b = a.state + ((size_t)h * D + row0 + (has_b ? rb : 0)) * D;
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+        float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+        if (has_a) va = *reinterpret_cast<const float4 *>(srow_a + CSTRIDE * i + 4 * j);
+        if (has_b) vb = *reinterpret_cast<const float4 *>(srow_b + CSTRIDE * i + 4 * j);
+        Sa[2 * i] = make_float2(va.x, va.y); Sa[2 * i + 1] = make_float2(va.z, va.w);
+        Sb[2 * i] = make_float2(vb.x, vb.y); Sb[2 * i + 1] = make_float2(vb.z, vb.w);
+        if (RECORD && has_a)
+            *reinterpret_cast<float4 *>(a.saved_state + (srow_a - a.state) + CSTRIDE * i + 4 * j) = va;
+        if (RECORD && has_b)
+            *reinterpret_cast<float4 *>(a.saved_state + (srow_b - a.state) + CSTRIDE * i + 4 * j) = vb;
+    }
 
     for (int t0 = 0, chunk = 0; t0 < a.T; t0 += CHUNK, ++chunk) {
         const int n = min(CHUNK, a.T - t0);
@@ -194,7 +225,7 @@ delta_kernel(const DeltaArgs a) {
                 float v = w3 * f;
                 v += w0 * h0; v += w1 * h1; v += w2 * h2;
                 h0 = h1; h1 = h2; h2 = f;
-                f = siluf_(v);
+                f = silu_fast(v);
             }
             sq2[tt] = 0.f;
             if (c >= 0 && tt < n) {
@@ -211,6 +242,7 @@ delta_kernel(const DeltaArgs a) {
             }
         }
         __syncthreads();
+        if (tid == 0 && chunk == 0) QV_STAMP(3);
         if (tid < n) {
             float qs = 0.f, ks = 0.f;
 #pragma unroll
@@ -218,7 +250,7 @@ delta_kernel(const DeltaArgs a) {
             scal[tid][0] = rsqrtf(qs + 1e-6f) * rsqrtf((float)D);
             scal[tid][1] = rsqrtf(ks + 1e-6f);
             scal[tid][2] = expf(decay_h * softplusf_(al + bias_h));
-            scal[tid][3] = sigmoidf_(be);
+            scal[tid][3] = sigmoid_fast(be);
         }
         // k.q of each token (filtered, not normalised), one warp per token
         for (int tt = warp; tt < n; tt += NW) {
@@ -229,6 +261,7 @@ delta_kernel(const DeltaArgs a) {
             if (lane == 0) scal[tt][4] = x;
         }
         __syncthreads();
+        if (tid == 0 && chunk == 0) QV_STAMP(4);
         if (RECORD) {
             // transition trace (recorded calls have a single chunk)
             if (owns_channel) {
@@ -262,50 +295,68 @@ delta_kernel(const DeltaArgs a) {
                 const float4 *kk = reinterpret_cast<const float4 *>(Fk[tt]);
                 const float4 *qq = reinterpret_cast<const float4 *>(Fq[tt]);
                 float4 k4[NV4];
-                float ua0 = 0.f, ua1 = 0.f, ub0 = 0.f, ub1 = 0.f, wa0 = 0.f, wa1 = 0.f, wb0 = 0.f, wb1 = 0.f;
+                float2 ua2 = make_float2(0.f, 0.f), ub2 = ua2, wa2 = ua2, wb2 = ua2;
 #pragma unroll
                 for (int i = 0; i < NV4; ++i) {
-                    k4[i] = kk[8 * i + j];
-                    const float4 q4 = qq[8 * i + j];
-                    ua0 = fmaf(Sa[4 * i], k4[i].x, ua0); ua1 = fmaf(Sa[4 * i + 1], k4[i].y, ua1);
-                    ua0 = fmaf(Sa[4 * i + 2], k4[i].z, ua0); ua1 = fmaf(Sa[4 * i + 3], k4[i].w, ua1);
-                    ub0 = fmaf(Sb[4 * i], k4[i].x, ub0); ub1 = fmaf(Sb[4 * i + 1], k4[i].y, ub1);
-                    ub0 = fmaf(Sb[4 * i + 2], k4[i].z, ub0); ub1 = fmaf(Sb[4 * i + 3], k4[i].w, ub1);
-                    wa0 = fmaf(Sa[4 * i], q4.x, wa0); wa1 = fmaf(Sa[4 * i + 1], q4.y, wa1);
-                    wa0 = fmaf(Sa[4 * i + 2], q4.z, wa0); wa1 = fmaf(Sa[4 * i + 3], q4.w, wa1);
-                    wb0 = fmaf(Sb[4 * i], q4.x, wb0); wb1 = fmaf(Sb[4 * i + 1], q4.y, wb1);
-                    wb0 = fmaf(Sb[4 * i + 2], q4.z, wb0); wb1 = fmaf(Sb[4 * i + 3], q4.w, wb1);
+                    k4[i] = kk[TPP * i + j];
+                    const float4 q4 = qq[TPP * i + j];
+                    const float2 kl = make_float2(k4[i].x, k4[i].y), kh = make_float2(k4[i].z, k4[i].w);
+                    const float2 ql = make_float2(q4.x, q4.y), qh = make_float2(q4.z, q4.w);
+                    ua2 = ffma2(Sa[2 * i], kl, ua2); ua2 = ffma2(Sa[2 * i + 1], kh, ua2);
+                    ub2 = ffma2(Sb[2 * i], kl, ub2); ub2 = ffma2(Sb[2 * i + 1], kh, ub2);
+                    wa2 = ffma2(Sa[2 * i], ql, wa2); wa2 = ffma2(Sa[2 * i + 1], qh, wa2);
+                    wb2 = ffma2(Sb[2 * i], ql, wb2); wb2 = ffma2(Sb[2 * i + 1], qh, wb2);
                 }
+                const float ua0 = ua2.x, ua1 = ua2.y, ub0 = ub2.x, ub1 = ub2.y;
+                const float wa0 = wa2.x, wa1 = wa2.y, wb0 = wb2.x, wb1 = wb2.y;
                 const float ua = ua0 + ua1, ub = ub0 + ub1, wa = wa0 + wa1, wb = wb0 + wb1;
-                const bool hi4 = (j & 4) != 0, hi2 = (j & 2) != 0;
-                float m0 = hi4 ? wa : ua, m1 = hi4 ? wb : ub;
-                m0 += __shfl_xor_sync(0xffffffffu, hi4 ? ua : wa, 4);
-                m1 += __shfl_xor_sync(0xffffffffu, hi4 ? ub : wb, 4);
-                float m = hi2 ? m1 : m0;
-                m += __shfl_xor_sync(0xffffffffu, hi2 ? m0 : m1, 2);
-                m += __shfl_xor_sync(0xffffffffu, m, 1);
-                // delta of row a on lanes 0-1, of row b on lanes 2-3; broadcast to the pair
-                const int rl = hi2 ? rb : ra;
+                // Transposing butterfly over the pair's TPP lanes: afterwards the
+                // lanes of the first quarter hold S_a.k, the second S_b.k, the
+                // third S_a.q, the fourth S_b.q (each the full 128-column sum).
+                float m;
+                bool hq;                                   // this lane's sum is of row b
+                if (TPP == 16) {
+                    const bool h8 = (j & 8) != 0;
+                    hq = (j & 4) != 0;
+                    float x0 = h8 ? wa : ua, x1 = h8 ? wb : ub;
+                    x0 += __shfl_xor_sync(0xffffffffu, h8 ? ua : wa, 8);
+                    x1 += __shfl_xor_sync(0xffffffffu, h8 ? ub : wb, 8);
+                    m = hq ? x1 : x0;
+                    m += __shfl_xor_sync(0xffffffffu, hq ? x0 : x1, 4);
+                    m += __shfl_xor_sync(0xffffffffu, m, 2);
+                    m += __shfl_xor_sync(0xffffffffu, m, 1);
+                } else {
+                    const bool hi4 = (j & 4) != 0;
+                    hq = (j & 2) != 0;
+                    float m0 = hi4 ? wa : ua, m1 = hi4 ? wb : ub;
+                    m0 += __shfl_xor_sync(0xffffffffu, hi4 ? ua : wa, 4);
+                    m1 += __shfl_xor_sync(0xffffffffu, hi4 ? ub : wb, 4);
+                    m = hq ? m1 : m0;
+                    m += __shfl_xor_sync(0xffffffffu, hq ? m0 : m1, 2);
+                    m += __shfl_xor_sync(0xffffffffu, m, 1);
+                }
+                // delta of row a on the first quarter's lanes, of row b on the
+                // second's; broadcast to the pair
+                const int rl = hq ? rb : ra;
                 const float vrow = rl < rows ? Fv[tt][rl] : 0.f;
                 const float dl = (vrow - decay * m * skn) * beta * skn;
-                const int base = lane & ~7;
-                const float da = __shfl_sync(0xffffffffu, dl, base), db = __shfl_sync(0xffffffffu, dl, base + 2);
-                // readout of row a on lane 4, of row b on lane 6
-                if ((j == 4 || j == 6) && rl < rows) O[tt][rl] = sqn * fmaf(decay, m, (hi2 ? db : da) * kq);
+                const int base = lane & ~(TPP - 1);
+                const float da = __shfl_sync(0xffffffffu, dl, base), db = __shfl_sync(0xffffffffu, dl, base + TPP / 4);
+                // readout of row a / b on the first lane of the third / fourth quarter
+                if ((j == TPP / 2 || j == 3 * TPP / 4) && rl < rows) O[tt][rl] = sqn * fmaf(decay, m, (hq ? db : da) * kq);
+                const float2 dec2 = make_float2(decay, decay), da2 = make_float2(da, da), db2 = make_float2(db, db);
 #pragma unroll
                 for (int i = 0; i < NV4; ++i) {
-                    Sa[4 * i] = fmaf(Sa[4 * i], decay, k4[i].x * da);
-                    Sa[4 * i + 1] = fmaf(Sa[4 * i + 1], decay, k4[i].y * da);
-                    Sa[4 * i + 2] = fmaf(Sa[4 * i + 2], decay, k4[i].z * da);
-                    Sa[4 * i + 3] = fmaf(Sa[4 * i + 3], decay, k4[i].w * da);
-                    Sb[4 * i] = fmaf(Sb[4 * i], decay, k4[i].x * db);
-                    Sb[4 * i + 1] = fmaf(Sb[4 * i + 1], decay, k4[i].y * db);
-                    Sb[4 * i + 2] = fmaf(Sb[4 * i + 2], decay, k4[i].z * db);
-                    Sb[4 * i + 3] = fmaf(Sb[4 * i + 3], decay, k4[i].w * db);
+                    const float2 kl = make_float2(k4[i].x, k4[i].y), kh = make_float2(k4[i].z, k4[i].w);
+                    Sa[2 * i] = ffma2(kl, da2, fmul2(Sa[2 * i], dec2));
+                    Sa[2 * i + 1] = ffma2(kh, da2, fmul2(Sa[2 * i + 1], dec2));
+                    Sb[2 * i] = ffma2(kl, db2, fmul2(Sb[2 * i], dec2));
+                    Sb[2 * i + 1] = ffma2(kh, db2, fmul2(Sb[2 * i + 1], dec2));
                 }
             }
         }
         __syncthreads();
+        if (tid == 0 && chunk == 0) QV_STAMP(5);
         if (CORE) {
             if (has_out && out_t < n) a.out[((size_t)(t0 + out_t) * Hv + h) * D + row0 + out_i] = O[out_t][out_i];
         } else {
@@ -325,13 +376,14 @@ delta_kernel(const DeltaArgs a) {
             }
             if (tid == 0) norm_ok = mbar_wait_cluster(&osum_bar[par], (uint32_t)(chunk >> 1) & 1);
             __syncthreads();
+            if (tid == 0 && chunk == 0) QV_STAMP(6);
             if (norm_ok && has_out && out_t < n) {
                 float total = 0.f;
 #pragma unroll
                 for (int q = 0; q < CPH; ++q) total += osum[par][q][out_t];
                 const float scale = rsqrtf(total / D + a.eps);
                 a.out[((size_t)(t0 + out_t) * Hv + h) * D + row0 + out_i] =
-                    O[out_t][out_i] * scale * nw * siluf_(gz);
+                    O[out_t][out_i] * scale * nw * silu_fast(gz);
             }
         }
         __syncthreads();
@@ -340,17 +392,18 @@ delta_kernel(const DeltaArgs a) {
 #pragma unroll
     for (int i = 0; i < NV4; ++i) {
         if (has_a)
-            *reinterpret_cast<float4 *>(srow_a + 32 * i + 4 * j) =
-                make_float4(Sa[4 * i], Sa[4 * i + 1], Sa[4 * i + 2], Sa[4 * i + 3]);
+            *reinterpret_cast<float4 *>(srow_a + CSTRIDE * i + 4 * j) =
+                make_float4(Sa[2 * i].x, Sa[2 * i].y, Sa[2 * i + 1].x, Sa[2 * i + 1].y);
         if (has_b)
-            *reinterpret_cast<float4 *>(srow_b + 32 * i + 4 * j) =
-                make_float4(Sb[4 * i], Sb[4 * i + 1], Sb[4 * i + 2], Sb[4 * i + 3]);
+            *reinterpret_cast<float4 *>(srow_b + CSTRIDE * i + 4 * j) =
+                make_float4(Sb[2 * i].x, Sb[2 * i].y, Sb[2 * i + 1].x, Sb[2 * i + 1].y);
     }
     // History: v channels belong to their rows' CTA; the q/k channels of key
     // head kh are written by rank 0 of value head kh (h < Hk) only.
     if (!CORE && c >= 0 && (e >= 2 * D || (h < Hk && rank == 0))) {
         a.history[c] = h0; a.history[(size_t)C + c] = h1; a.history[2 * (size_t)C + c] = h2;
     }
+    if (tid == 0) QV_STAMP(7);
 }
 
 // Commit of a recorded verify call after `accepted` of its tokens were kept
