@@ -27,6 +27,8 @@ import sys
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
@@ -130,7 +132,7 @@ class ClockSampler:
 class Step:
     """Device-resident buffers of the 64 layers and the per-step dispatch."""
 
-    def __init__(self, hot, context, tokens, rank, world, seed=1234):
+    def __init__(self, hot, context, tokens, rank, world, seed=1234, attention_only=False):
         import torch
         self.torch, self.hot = torch, hot
         self.dev = torch.device('cuda', torch.cuda.current_device())
@@ -146,6 +148,8 @@ class Step:
         f32 = dict(device=self.dev, dtype=torch.float32)
         self.attn, self.delta = [], []
         for layer in range(LAYERS):
+            if attention_only and layer % 4 != 3:
+                continue
             if layer % 4 == 3:
                 kc = torch.randn((cap, HKV, HD), generator=g, device=self.dev, dtype=torch.float16)
                 vc = torch.randn((cap, HKV, HD), generator=g, device=self.dev, dtype=torch.float16)
@@ -203,6 +207,11 @@ class Step:
             dist.all_gather_into_tensor(self.glse.view(-1, H), self.lse)
             hot.attention_merge(a['out'], self.gpart, self.glse, self.world, T, a['q_gate'])
 
+    def attention_only(self):
+        """The step's attention layers back to back (what the attention scaling figure times)."""
+        for ai, a in enumerate(self.attn):
+            self.attention_layer(a, seq=ai)
+
     def delta_layer(self, d):
         self.hot.delta(d['out'], d['state'], d['history'], d['qkv'], d['gate'], d['alpha'], d['beta'], d['conv'],
                        self.decay, self.bias, self.norm, self.T, HK, HV, DK)
@@ -223,7 +232,10 @@ class Step:
 
     # host-side (pinned) copies of the per-step inputs and outputs, for e2e
     def host_mirror(self):
+        """Pinned host copies of every layer's inputs (each rank feeds its own GPU) and of every
+        layer's output (read back by rank 0 only: the outputs are identical on every rank)."""
         torch = self.torch
+        self.readback = self.rank == 0
         self.h_in_attn, self.h_in_delta, self.h_out_attn, self.h_out_delta = [], [], [], []
         for a in self.attn:
             self.h_in_attn.append([(a[k], a[k].cpu().pin_memory()) for k in ('q_gate', 'key', 'value')])
@@ -272,11 +284,12 @@ class Step:
                 self.delta_layer(self.delta[di])
                 dev, host = self.h_out_delta[di]
                 di += 1
-            done = torch.cuda.Event()
-            done.record(main)
-            self.s_out.wait_event(done)
-            with torch.cuda.stream(self.s_out):
-                host.copy_(dev, non_blocking=True)
+            if self.readback:
+                done = torch.cuda.Event()
+                done.record(main)
+                self.s_out.wait_event(done)
+                with torch.cuda.stream(self.s_out):
+                    host.copy_(dev, non_blocking=True)
         main.wait_stream(self.s_in)
         main.wait_stream(self.s_out)
 
@@ -285,6 +298,25 @@ def make_events(n, external):
     import torch
     return [(torch.cuda.Event(enable_timing=True, external=external),
              torch.cuda.Event(enable_timing=True, external=external)) for _ in range(n)]
+
+
+def time_graph(torch, fn, reps, warmup, sync=None):
+    """Mean device time (ms) of one replay of a CUDA graph of fn()."""
+    graph = capture(torch, fn)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if sync is not None:
+        sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    graph.reset()
+    return ms
 
 
 def capture(torch, fn):
@@ -418,7 +450,24 @@ def bench_b200(args):
         barrier()
         e_ms = max_over_ranks([e0.elapsed_time(e1) / K])[0]
         e2e = {'value': round(e_ms * 1e3, 2), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
-               'd2h_bytes_per_step': d2h, 'launch': 'cuda-graph' if e2e_graph is not None else 'eager'}
+               'd2h_bytes_per_step': d2h, 'launch': 'cuda-graph' if e2e_graph is not None else 'eager',
+               'copies': 'every rank copies its own inputs; rank 0 reads back every layer\'s output'}
+
+    # The attention layers back to back (the sequence split's own figure, free of the replicated
+    # DeltaNet layers): every rank times its shards; at N > 1 rank 0 also times the same 16 layers
+    # at the full context on its one GPU, so that the scaling efficiency t1 / (N tN) comes from
+    # one run on one box.
+    attn_b2b = attn_1 = None
+    if not args.no_extras:
+        attn_b2b = max_over_ranks([time_graph(torch, step.attention_only, K, args.warmup, barrier)
+                                   / len(step.attn)])[0]
+        if world > 1:
+            if rank == 0:
+                full = Step(hot, args.context, args.tokens, 0, 1, seed=99, attention_only=True)
+                attn_1 = time_graph(torch, full.attention_only, K, args.warmup) / len(full.attn)
+                del full
+                torch.cuda.empty_cache()
+            barrier()
 
     hbm_peak, tc_peak, peak_kind = peaks()
     kv_rows = step.rows + (args.tokens if step.last else 0)
@@ -440,6 +489,12 @@ def bench_b200(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.context, args.tokens)
 
+    per_layer = {'attention': round(attn_ms * 1e3, 2), 'delta_estimate': round((ms - 16 * attn_ms) * 1e3 / 48, 2)}
+    if attn_b2b is not None:
+        per_layer['attention_back_to_back'] = round(attn_b2b * 1e3, 2)
+    if attn_1 is not None:
+        per_layer['attention_back_to_back_1gpu'] = round(attn_1 * 1e3, 2)
+        per_layer['attention_scaling_eff'] = round(attn_1 / (world * attn_b2b), 4)
     if rank == 0:
         line = {
             'metric': METRIC, 'value': round(ms * 1e3, 2), 'unit': UNIT, 'n_gpus': world, 'steps': K,
@@ -460,8 +515,7 @@ def bench_b200(args):
             'e2e': e2e,
             'roofline': roofline,
             'cpu_baseline': cpu,
-            'per_layer_us': {'attention': round(attn_ms * 1e3, 2),
-                             'delta_estimate': round((ms - 16 * attn_ms) * 1e3 / 48, 2)},
+            'per_layer_us': per_layer,
             'extras': extras,
         }
         emit(line)
@@ -654,47 +708,101 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
 
 
 # ----------------------------------------------------------------------------- CPU
-def cpu_sample(context, tokens, attn_layers=1, delta_layers=3, seed=4321):
-    """Time the CPU oracle on 1 attention + 3 DeltaNet layers (1/16 of a step)."""
-    import oracle
-    from oracle import inputs as I
-    a = I.attention_layer(batch=tokens, position=context - tokens, seed=seed)
-    d = [I.delta_layer(batch=tokens, seed=seed + 1 + i) for i in range(delta_layers)]
-    t = time.perf_counter()
-    for _ in range(attn_layers):
-        oracle.attention(**a)
-    for c in d:
-        oracle.delta(**c)
-    dt = time.perf_counter() - t
-    return dt * (16 / attn_layers)
+class CpuStep:
+    """The same verify step on the host cores: the C restatement of the oracle (float64,
+    oracle/c/qv_oracle.c, pinned to the reference's cpu_reference.py outputs by the tests),
+    16 attention layers at the full context + 48 DeltaNet layers, every layer computed.
+
+    The 16 attention layers share one prefix cache (570 MB of fp16 at context 139,264; every
+    layer streams all of it, as a layer with its own cache would), each with its own inputs; the
+    48 DeltaNet layers keep their own float64 states."""
+
+    def __init__(self, context, tokens, threads, seed=4321):
+        from oracle import inputs as I
+        from oracle import native
+        native.build()
+        self.native, self.T, self.threads = native, tokens, threads
+        self.position = context - tokens
+        a = I.attention_layer(batch=tokens, position=self.position, seed=seed)
+        n = context
+        self.kc = np.zeros((n, HKV, HD), np.float16)
+        self.vc = np.zeros_like(self.kc)
+        self.kc[:self.position] = a['key_cache'][:self.position]
+        self.vc[:self.position] = a['value_cache'][:self.position]
+        rng = np.random.default_rng(seed)
+        self.attn = [dict(q_gate=rng.standard_normal((tokens, H, 2 * HD), dtype=np.float32),
+                          key=rng.standard_normal((tokens, HKV, HD), dtype=np.float32),
+                          value=rng.standard_normal((tokens, HKV, HD), dtype=np.float32)) for _ in range(16)]
+        self.ones = np.ones(HD, np.float32)
+        self.delta = [I.delta_layer(batch=tokens, seed=seed + 1 + i) for i in range(48)]
+        for d in self.delta:
+            d['state'] = np.asarray(d['state'], np.float64).reshape(-1).copy()
+            d['history'] = np.asarray(d['history'], np.float64).reshape(-1).copy()
+
+    def run(self):
+        """One step (the state and history of every DeltaNet layer advance, as on the GPU)."""
+        nat, T = self.native, self.T
+        for layer in range(LAYERS):
+            if layer % 4 == 3:
+                x = self.attn[layer // 4]
+                nat.attention(self.kc, self.vc, x['q_gate'], x['key'], x['value'], self.ones, self.ones, T,
+                              self.position, 1e-6, threads=self.threads, caches_in_place=True)
+            else:
+                d = self.delta[layer - layer // 4 - 1]
+                _, d['state'], d['history'] = nat.delta(**d, threads=self.threads)
+
+    def time_config(self, which):
+        """Single-threaded time of BASELINE configuration 0 (attention, context 136) or 1 (DeltaNet)."""
+        from oracle import inputs as I
+        nat = self.native
+        c = I.attention_layer(batch=8, position=128) if which == 0 else I.delta_layer(batch=8)
+        fn = (lambda: nat.attention(**c, threads=1)) if which == 0 else (lambda: nat.delta(**c, threads=1))
+        fn()
+        t = time.perf_counter()
+        reps = 20
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t) / reps
 
 
-def cpu_threads():
-    try:
-        import threadpoolctl
-        info = threadpoolctl.threadpool_info()
-        return max(i.get('num_threads', 1) for i in info) if info else 1
-    except Exception:
-        return os.cpu_count() or 1
+def host_threads():
+    return len(os.sched_getaffinity(0)) if hasattr(os, 'sched_getaffinity') else (os.cpu_count() or 1)
 
 
 def cpu_baseline(context, tokens):
-    seconds = cpu_sample(context, tokens)
-    return {'value': round(seconds * 1e6, 1), 'unit': UNIT, 'cores': cpu_threads(), 'kind': 'port',
-            'sample': f'numpy float64 restatement of cpu_reference.py on 1 attention layer (ctx {context}, '
-                      f'verify-{tokens}) + 3 DeltaNet layers = 1/16 of a step, scaled x16; '
-                      f'BLAS threads = cores; host has {os.cpu_count()} cpus'}
+    """One full step of the C restatement on all host threads (no sampling, no scaling), and the
+    single-threaded times of configurations 0 and 1."""
+    threads = host_threads()
+    step = CpuStep(context, tokens, threads)
+    step.run()                                   # warm (page-in of the cache, thread start-up)
+    t = time.perf_counter()
+    step.run()
+    seconds = time.perf_counter() - t
+    return {'value': round(seconds * 1e6, 1), 'unit': UNIT, 'cores': threads, 'kind': 'port',
+            'sample': f'one whole step: 16 attention layers at context {context} (verify-{tokens}) + 48 '
+                      f'DeltaNet layers, float64 C restatement of cpu_reference.py on {threads} host threads '
+                      f'(host has {os.cpu_count()} cpus)',
+            'configs_single_thread_us': {'cfg0_attention_ctx136': round(step.time_config(0) * 1e6, 1),
+                                         'cfg1_deltanet': round(step.time_config(1) * 1e6, 1)}}
 
 
 def bench_reference(args):
+    """The reference arm: the path's CPU implementation (the C restatement of the reference's
+    cpu_reference.py; the reference's own is Python, which does not travel to the GPU box) timed
+    on whole steps: args.warmup untimed steps, then args.steps timed ones, all on rank 0."""
     rank = int(os.environ.get('RANK', 0))
     if rank != 0:
         return
-    for _ in range(min(args.warmup, 1)):
-        cpu_sample(args.context, args.tokens)
-    times = [cpu_sample(args.context, args.tokens) for _ in range(args.steps)]
-    value = statistics.median(times) * 1e6
-    cores = cpu_threads()
+    threads = host_threads()
+    step = CpuStep(args.context, args.tokens, threads)
+    for _ in range(args.warmup):
+        step.run()
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        step.run()
+        times.append(time.perf_counter() - t)
+    value = statistics.mean(times) * 1e6
     line = {
         'metric': METRIC, 'value': round(value, 1), 'unit': UNIT, 'n_gpus': int(os.environ.get('WORLD_SIZE', 1)),
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(value / 1e3, 3),
@@ -703,10 +811,11 @@ def bench_reference(args):
         'config': {'workload': f'verify-{args.tokens} hot-path step of the 64-layer model: 16 attention '
                                f'layers at context {args.context} + 48 gated-DeltaNet layers',
                    'context': args.context, 'verify_tokens': args.tokens},
-        'cpu_baseline': {'value': round(value, 1), 'unit': UNIT, 'cores': cores, 'kind': 'port',
-                         'sample': 'CPU oracle (numpy float64 restatement of the reference cpu_reference.py; '
-                                   'the reference itself is Python and cannot travel) on 1 attention + 3 '
-                                   'DeltaNet layers per step, scaled x16 to the 64-layer step'},
+        'cpu_baseline': {'value': round(value, 1), 'unit': UNIT, 'cores': threads, 'kind': 'port',
+                         'sample': f'whole steps ({args.warmup} warm-up + {args.steps} timed, all run): the float64 '
+                                   f'C restatement of the reference cpu_reference.py (oracle/c/qv_oracle.c) on '
+                                   f'{threads} host threads; the reference itself is Python and does not travel'},
+        'timed_seconds': round(sum(times), 2),
         'e2e': {'value': round(value, 1), 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     emit(line)
