@@ -613,6 +613,45 @@ def side_measurements(hot, torch, tc_peak, hbm_peak):
     torch.cuda.synchronize()
     res['delta_prefill_4096_recurrent_us'] = round(e0.elapsed_time(e1) * 1e3, 2)
     del ws, qd, kd, vd, od
+    # the layer-level prefills with the reference's layer semantics at 4096 tokens: the DeltaNet layer
+    # (conv + SiLU, norms, chunked recurrence, gated RMSNorm: qv_delta_prefill) and the attention layer
+    # (RMSNorm + rotary + fp16 append, PRECISE causal attention, gate: qv_attention's prefill regime)
+    C_ = (2 * HK + HV) * DK
+    f32 = dict(device='cuda', dtype=torch.float32)
+    lp = dict(state=torch.zeros((HV, DK, DK), **f32), history=torch.zeros((3, C_), **f32),
+              qkv=torch.randn((L, C_), generator=g, **f32), gate=torch.randn((L, HV, DK), generator=g, **f32),
+              alpha=torch.randn((L, HV), generator=g, **f32), beta=torch.randn((L, HV), generator=g, **f32),
+              conv=torch.randn((C_, 4), generator=g, **f32) * 0.5, decay=dec, bias=bia, norm=torch.ones(DK, **f32))
+    lout = torch.empty((L, HV, DK), **f32)
+    lws = torch.empty(hot.lib.qv_delta_prefill_workspace(L, HK, HV), dtype=torch.uint8, device='cuda')
+    for _ in range(2):
+        hot.delta_prefill(lout, **lp, tokens=L, key_heads=HK, value_heads=HV, dim=DK, workspace=lws)
+    e0.record()
+    for _ in range(5):
+        hot.delta_prefill(lout, **lp, tokens=L, key_heads=HK, value_heads=HV, dim=DK, workspace=lws)
+    e1.record()
+    torch.cuda.synchronize()
+    res['delta_layer_prefill_4096_us'] = round(e0.elapsed_time(e1) / 5 * 1e3, 2)
+    del lp, lout, lws
+    kc = torch.zeros((L, HKV, HD), device='cuda', dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    qg = torch.randn((L, H, 2 * HD), generator=g, **f32)
+    ky = torch.randn((L, HKV, HD), generator=g, **f32)
+    vl = torch.randn((L, HKV, HD), generator=g, **f32)
+    ao = torch.empty((L, H, HD), **f32)
+    ones = torch.ones(HD, **f32)
+    aws = torch.zeros(hot.lib.qv_attention_workspace(L, 0), dtype=torch.uint8, device='cuda')
+    for _ in range(2):
+        hot.attention(ao, kc, vc, qg, ky, vl, ones, ones, L, 0, workspace=aws)
+    e0.record()
+    for _ in range(5):
+        hot.attention(ao, kc, vc, qg, ky, vl, ones, ones, L, 0, workspace=aws)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 5
+    res['attention_layer_prefill_4096_us'] = round(ms * 1e3, 2)
+    res['attention_layer_prefill_tflops'] = round(flops / (ms * 1e-3) / 1e12, 1)
+    del kc, vc, qg, ky, vl, ao, aws
     # verify/commit transaction: 48 DeltaNet layers with distinct states,
     # plain layer vs recorded verify, and the commit of 3 of 8 tokens, each replayed as a graph
     T8, C_ = 8, (2 * HK + HV) * DK

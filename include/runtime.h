@@ -259,6 +259,27 @@ int qv_delta_chunked(float *out, float *state, const void *q, const void *k, con
                      int tokens, int key_heads, int value_heads, int dim,
                      void *workspace, size_t workspace_bytes, void *stream);
 
+/* Gated-DeltaNet layer prefill in the chunked form (device memory,
+ * asynchronous on `stream`): the layer of qv_delta -- causal conv + SiLU over
+ * the conv history and the block, q / k L2 norms, the delta rule, gated
+ * RMSNorm, history updated to the block's last three raw rows -- over a long
+ * block of tokens, with the recurrence evaluated in chunks of 64 tokens on
+ * the tensor cores (qv_delta_chunked).  Same arguments and layouts as
+ * qv_delta; dim must be 128.  The filtered q, k, v enter the tensor cores as
+ * fp16, which bounds the state at ~1e-3 relative (not qv_delta's float32
+ * level) over thousands of tokens; qv_delta stays the exact recurrence.
+ * `workspace`: caller-owned device memory of at least
+ * qv_delta_prefill_workspace(tokens, key_heads, value_heads) bytes (0 =
+ * invalid arguments), contents need not be initialised. */
+size_t qv_delta_prefill_workspace(int tokens, int key_heads, int value_heads);
+int qv_delta_prefill(float *out, float *state, float *history,
+                     const float *qkv, const float *gate,
+                     const float *alpha, const float *beta,
+                     const float *conv, const float *decay,
+                     const float *bias, const float *norm,
+                     int tokens, int key_heads, int value_heads, int dim,
+                     float epsilon, void *workspace, size_t workspace_bytes, void *stream);
+
 /* qv_attention without a workspace argument, for callers that cannot
  * allocate device memory (no counterpart in the reference ABI).  A serving
  * runtime that gave all of HBM to its own pools at start-up, or a plugin host

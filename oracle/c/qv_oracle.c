@@ -304,10 +304,13 @@ static void delta_head(void *p, int h) {
 
 /* One gated-DeltaNet layer over `batch` tokens: out [batch][Hv][dim], state
  * [Hv][dim][dim] and history [3][C] (in/out) in float64; inputs as the
- * reference ABI passes them (float32).  Returns 0, or -1 on invalid arguments. */
+ * reference ABI passes them (float32).  With `round_filtered` the conv + SiLU
+ * outputs are rounded to binary16 before anything else uses them (a model of
+ * a kernel that takes them as fp16 operands; the reference does not round).
+ * Returns 0, or -1 on invalid arguments. */
 int qvo_delta(double *out, double *state, double *history, const float *qkv, const float *gate, const float *alpha,
               const float *beta, const float *conv, const float *decay, const float *bias, const float *norm,
-              int batch, int key_heads, int value_heads, int dim, double epsilon, int threads) {
+              int batch, int key_heads, int value_heads, int dim, double epsilon, int threads, int round_filtered) {
     if (batch < 1 || key_heads < 1 || value_heads < key_heads || value_heads % key_heads || dim < 1 || !out || !state ||
         !history || !qkv || !gate || !alpha || !beta || !conv || !decay || !bias || !norm)
         return -1;
@@ -323,6 +326,7 @@ int qvo_delta(double *out, double *state, double *history, const float *qkv, con
             double acc = 0.0;
             for (int j = 0; j < 3; ++j) acc += (double)conv[4 * ch + j] * history[(size_t)j * C + ch];
             f[ch] = silu(acc + (double)conv[4 * ch + 3] * (double)raw[ch]);
+            if (round_filtered) f[ch] = half_to_double(double_to_half((double)(float)f[ch]));
         }
         memmove(history, history + C, sizeof(double) * 2 * C);   /* history = history[C:] + raw */
         for (int ch = 0; ch < C; ++ch) history[2 * (size_t)C + ch] = (double)raw[ch];

@@ -43,7 +43,7 @@ def load():
         P, I, D = ct.c_void_p, ct.c_int, ct.c_double
         lib.qvo_attention.argtypes = [P] * 8 + [I, I, D, I]
         lib.qvo_attention.restype = I
-        lib.qvo_delta.argtypes = [P] * 11 + [I, I, I, I, D, I]
+        lib.qvo_delta.argtypes = [P] * 11 + [I, I, I, I, D, I, I]
         lib.qvo_delta.restype = I
         _lib = lib
     return _lib
@@ -85,14 +85,16 @@ def attention(key_cache, value_cache, q_gate, key, value, q_norm, k_norm, batch,
 
 
 def delta(state, history, qkv, gate, alpha, beta, conv, decay, bias, norm, batch, key_heads, value_heads, dim,
-          epsilon, threads=None):
-    """cpu_reference.delta: returns (out, state, history) as float64 flat arrays."""
+          epsilon, threads=None, round_filtered=False):
+    """cpu_reference.delta: returns (out, state, history) as float64 flat arrays.  With
+    ``round_filtered`` the conv + SiLU outputs are rounded to fp16 first (a model of a kernel that
+    takes them as fp16 operands, as the chunked layer prefill does; the reference does not round)."""
     st = np.array(state, np.float64).reshape(-1).copy()
     hi = np.array(history, np.float64).reshape(-1).copy()
     out = np.empty(batch * value_heads * dim, np.float64)
     args = [_f32(x) for x in (qkv, gate, alpha, beta, conv, decay, bias, norm)]
     rc = load().qvo_delta(_ptr(out), _ptr(st), _ptr(hi), *map(_ptr, args), batch, key_heads, value_heads, dim,
-                          float(epsilon), threads or default_threads())
+                          float(epsilon), threads or default_threads(), int(bool(round_filtered)))
     if rc:
         raise ValueError('qvo_delta rejected its arguments')
     return out, st, hi

@@ -64,6 +64,14 @@ void delta_chunked(float *out, float *state, const __half *q, const __half *k, c
                    const float *beta, const float *decay, const float *bias, int T, int Hk, int Hv, int D, void *ws,
                    size_t ws_bytes, cudaStream_t st);
 
+// Gated-DeltaNet layer prefill in the chunked form (delta_prefill.cu): the
+// layer of delta_run (conv + SiLU with history, norms, delta rule, gated
+// RMSNorm) over T tokens, D = 128, with the recurrence on tcgen05.
+size_t delta_prefill_workspace_bytes(int T, int Hk, int Hv);
+void delta_prefill(float *out, float *state, float *history, const float *qkv, const float *gate, const float *alpha,
+                   const float *beta, const float *conv, const float *decay, const float *bias, const float *norm, int T,
+                   int Hk, int Hv, int D, float eps, void *ws, size_t ws_bytes, cudaStream_t st);
+
 // The thread-local message behind qv_error() (runtime.cu).
 void clear_error();
 void record_error(const char *message);

@@ -498,6 +498,31 @@ int qv_delta_core(float *out, float *state, const void *q, const void *k, const 
     });
 }
 
+size_t qv_delta_prefill_workspace(int tokens, int key_heads, int value_heads) {
+    if (tokens < 1 || tokens > kMaxContext || key_heads < 1 || value_heads < key_heads || value_heads > 48 ||
+        value_heads % key_heads)
+        return 0;
+    return qv::delta_prefill_workspace_bytes(tokens, key_heads, value_heads);
+}
+
+int qv_delta_prefill(float *out, float *state, float *history, const float *qkv, const float *gate, const float *alpha,
+                     const float *beta, const float *conv, const float *decay, const float *bias, const float *norm,
+                     int tokens, int key_heads, int value_heads, int dim, float epsilon, void *workspace,
+                     size_t workspace_bytes, void *stream) {
+    return guarded([&] {
+        require(tokens >= 1 && tokens <= kMaxContext, "tokens must be between 1 and 139264");
+        check_epsilon(epsilon);
+        check_delta_dims(key_heads, value_heads, dim);
+        require(dim == 128, "the chunked DeltaNet path needs dim 128");
+        require(out && state && history && qkv && gate && alpha && beta && conv && decay && bias && norm && workspace,
+                "null DeltaNet buffer");
+        require(workspace_bytes >= qv::delta_prefill_workspace_bytes(tokens, key_heads, value_heads),
+                "workspace too small");
+        qv::delta_prefill(out, state, history, qkv, gate, alpha, beta, conv, decay, bias, norm, tokens, key_heads,
+                          value_heads, dim, epsilon, workspace, workspace_bytes, as_stream(stream));
+    });
+}
+
 size_t qv_delta_chunked_workspace(int tokens, int value_heads) {
     if (tokens < 1 || tokens > kMaxContext || value_heads < 1 || value_heads > 48) return 0;
     return qv::delta_chunked_workspace_bytes(tokens, value_heads);

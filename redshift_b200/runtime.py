@@ -59,6 +59,8 @@ ADDITIVE_SIGNATURES = {
     'qv_delta_core': ([_P] * 9 + [_I] * 4 + [_P], _I),
     'qv_delta_chunked_workspace': ([_I, _I], _S),
     'qv_delta_chunked': ([_P] * 9 + [_I] * 4 + [_P, _S, _P], _I),
+    'qv_delta_prefill_workspace': ([_I, _I, _I], _S),
+    'qv_delta_prefill': ([_P] * 11 + [_I] * 4 + [_F, _P, _S, _P], _I),
     'qv_status': ([], _I),
     'qv_attention_noalloc': ([_P] * 8 + [_I, _I, _F, _P], _I),
 }
@@ -228,6 +230,20 @@ class HotPath:
         self.check(self.lib.qv_delta_chunked(p(out), p(state), p(q), p(k), p(v), p(alpha), p(beta), p(decay),
                                              p(bias), tokens, key_heads, value_heads, dim, p(workspace),
                                              workspace.numel() * workspace.element_size(), self._stream()))
+
+    def delta_prefill(self, out, state, history, qkv, gate, alpha, beta, conv, decay, bias, norm,
+                      tokens, key_heads, value_heads, dim, epsilon=1e-6, workspace=None):
+        """qv_delta_prefill: the DeltaNet layer over a long block in the chunked form; allocates the
+        workspace when none is given."""
+        p = self._ptr
+        need = self.lib.qv_delta_prefill_workspace(tokens, key_heads, value_heads)
+        if workspace is None:
+            import torch
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=out.device)
+        self.check(self.lib.qv_delta_prefill(p(out), p(state), p(history), p(qkv), p(gate), p(alpha), p(beta),
+                                             p(conv), p(decay), p(bias), p(norm), tokens, key_heads, value_heads,
+                                             dim, epsilon, p(workspace), workspace.numel() * workspace.element_size(),
+                                             self._stream()))
 
     def status(self):
         """Synchronise and return the kernel status word (0 = no timeout)."""
