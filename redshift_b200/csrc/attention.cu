@@ -232,8 +232,10 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 // (MAXS x 8 bytes): thread 0 brings both rows' blocks into shared memory
 // (`buf`, the idle K/V ring) with bulk copies on `bar` (phase parity
 // `phase`).  o[k] receives the normalised value of row k in dimension
-// threadIdx.x, lse[k] its natural-log LSE.  `sh` holds 2 MAXS + 8 floats of
-// shared memory; the call ends with a CTA barrier.
+// threadIdx.x, lse[k] its natural-log LSE.  `sh` holds 1280 floats of shared
+// memory (weights and maxima in the first 2 MAXS + 8, the exchange's words
+// after them, the rows' halves from float 256 on); the call ends with a CTA
+// barrier.
 __device__ bool combine_rows(const FaParams &p, int g, int ra, int rb, float *sh, float *buf, uint64_t *bar,
                              uint32_t phase, volatile int *abort_flag, float (&o)[2], float (&lse)[2]) {
     const int d = threadIdx.x, S = p.splits;
@@ -257,6 +259,7 @@ __device__ bool combine_rows(const FaParams &p, int g, int ra, int rb, float *sh
         }
     }
     const bool ok = mbar_wait(bar, phase, abort_flag);
+    if (threadIdx.x == 0 && phase == 0) QV_STAMP(14);
     // (max, sum) of split e of row a on threads [0, S), of row b on [64, 64 + S)
     const int e = d < 64 ? d : d - 64;
     float m = -INFINITY, l = 0.f;
@@ -278,14 +281,34 @@ __device__ bool combine_rows(const FaParams &p, int g, int ra, int rb, float *sh
     if (d < 128 && (d & 31) == 0) red[4 + (d >> 5)] = den_part;
     __syncthreads();
     const float den_a = red[4] + red[5], den_b = red[6] + red[7];
-    float aa[4] = {0.f, 0.f, 0.f, 0.f}, ab[4] = {0.f, 0.f, 0.f, 0.f};
-    if (ok) {
-        for (int k = 0; k < S; ++k) aa[k & 3] += wa[k] * xa[(size_t)k * HD + d];
-        if (two)
-            for (int k = 0; k < S; ++k) ab[k & 3] += wb[k] * xb[(size_t)k * HD + d];
+    // The weighted sum over the splits: thread (row, half, quad) reads four
+    // dimensions of its row with 16-byte loads over half of the splits; the
+    // two halves meet in shared memory.
+    const int rsel = d >> 7, hsel = (d >> 6) & 1, quad = d & 63;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ok && (rsel == 0 || two)) {
+        const float *x = rsel ? xb : xa, *w = rsel ? wb : wa;
+        const int k0 = hsel ? S / 2 : 0, k1 = hsel ? S : S / 2;
+        for (int k = k0; k < k1; ++k) {
+            const float4 v = *reinterpret_cast<const float4 *>(x + (size_t)k * HD + 4 * quad);
+            const float wk = w[k];
+            acc.x = fmaf(wk, v.x, acc.x); acc.y = fmaf(wk, v.y, acc.y);
+            acc.z = fmaf(wk, v.z, acc.z); acc.w = fmaf(wk, v.w, acc.w);
+        }
     }
-    o[0] = den_a > 0.f ? ((aa[0] + aa[1]) + (aa[2] + aa[3])) / den_a : 0.f;
-    o[1] = den_b > 0.f ? ((ab[0] + ab[1]) + (ab[2] + ab[3])) / den_b : 0.f;
+    float4 *part = reinterpret_cast<float4 *>(sh + 768);   // [2 rows][64 quads], the second halves
+    float *res = sh + 256;                                   // [2 rows][256], the normalised rows
+    if (hsel) part[rsel * 64 + quad] = acc;
+    __syncthreads();
+    if (!hsel) {
+        const float4 b = part[rsel * 64 + quad];
+        const float den = rsel ? den_b : den_a, inv = den > 0.f ? 1.f / den : 0.f;
+        *reinterpret_cast<float4 *>(res + rsel * HD + 4 * quad) =
+            make_float4((acc.x + b.x) * inv, (acc.y + b.y) * inv, (acc.z + b.z) * inv, (acc.w + b.w) * inv);
+    }
+    __syncthreads();
+    o[0] = res[d];
+    o[1] = res[HD + d];
     lse[0] = den_a > 0.f ? (Ma + log2f(den_a)) * LN2 : -INFINITY;
     lse[1] = den_b > 0.f ? (Mb + log2f(den_b)) * LN2 : -INFINITY;
     __syncthreads();                                   // sh and buf are free again
@@ -999,6 +1022,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                              warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag);
         if (o_ready) {
             tc_fence_after();
+            if (threadIdx.x == 128) QV_STAMP(12);
             const int chalf = warp < 4 ? 1 : 0;
             constexpr int RS = 128 * 4 + 16;                       // staging row bytes (padded)
             static_assert(8 * 32 * RS <= STAGES3 * L::SM_KV_STAGE, "O staging exceeds the K/V ring");
@@ -1019,6 +1043,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                             make_float4(o[q][e], o[q][e + 1], o[q][e + 2], o[q][e + 3]);
             }
             __syncwarp();
+            if (threadIdx.x == 128) QV_STAMP(13);
             const float *ml_s = reinterpret_cast<const float *>(smem + L::SM_ROPE);
             const bool direct = p.mode == 1;                       // prefill: final rows; decode: split partials
             // The valid logical rows of a CTA are a prefix, so are this warp's.
