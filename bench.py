@@ -41,7 +41,7 @@ LAYERS = 64
 # DRAM bytes (read + write) of one decode fa_kernel launch at context 139,264,
 # from `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` on
 # `python -m redshift_b200.profile_cases decode 139264` (profiles/fa_kernel_decode_139k.md).
-FA_TRAFFIC_139K = 570826240 + 3430912
+FA_TRAFFIC_139K = 570991360 + 199424
 
 
 RESULT_OUT = sys.stdout
