@@ -19,7 +19,7 @@ ROOT = Path(__file__).resolve().parents[1]
 CSRC = ROOT / 'redshift_b200' / 'csrc'
 BUILD = ROOT / 'build'
 LIBRARY = BUILD / 'libqvelox.so'
-SOURCES = ['status.cu', 'attention.cu', 'delta.cu', 'gdn_chunk.cu', 'delta_prefill.cu', 'projection.cu', 'copy.cu',
+SOURCES = ['status.cu', 'attention.cu', 'delta.cu', 'gdn_chunk.cu', 'delta_prefill.cu', 'prefill.cu', 'projection.cu', 'copy.cu',
            'runtime.cu', 'noalloc.cu']
 HEADERS = ['common.cuh', 'hotpath.h']
 

@@ -1,17 +1,16 @@
 // Full-attention hot path for sm_100a: prepare (RMSNorm + partial RoPE + fp16
 // KV append), a tcgen05/TMEM FlashAttention kernel that serves both the
 // decode/verify regime (split-KV, all 6 GQA heads x T tokens of one KV head
-// share every K/V tile) and causal prefill (a tile of query positions of one
-// head per CTA), and the split/shard combine kernels.
+// share every K/V tile) and the reference-semantics prefill regime (64 query
+// positions of one head per CTA), and the shard merge kernel.  The core-level
+// causal prefill with fp16 probabilities is prefill.cu.
 //
 // Semantics follow the reference's attn_prepare / attention / attention_tiled
 // (src/kernels.cu:415-503) and the CPU oracle tests/cpu_reference.py:55-89:
 // scores q.k/16 over cache rows [0, position+t], softmax, P.V, times
 // sigmoid(gate).
 //
-// Two precision modes of the FlashAttention kernel:
-//  * PRECISE (decode / verify and reference-semantics prefill): 64 query rows
-//    per CTA.  Q is split into fp16 hi = fp16(q) and lo = fp16(q - hi) and the
+// Precision: 64 query rows per CTA.  Q is split into fp16 hi = fp16(q) and lo = fp16(q - hi) and the
 //    QK MMA's A operand (held in TMEM) interleaves them: A row 32w+i = Q_hi and
 //    32w+16+i = Q_lo of query row 16w+i, so one M=128 MMA leaves both score
 //    halves of a row in lanes i and i+16 of warp w, which add them while they
@@ -19,7 +18,6 @@
 //    PV MMA's A rows 32w+i / 32w+16+i are P_hi / P_lo of row 16w+i, so O_hi and
 //    O_lo land in the same warp and are summed in the epilogue.  Scores and
 //    probabilities keep ~22 mantissa bits (the reference computes them in fp32).
-//  * FAST (core prefill, benchmark configuration 3): M=128 query rows and fp16 P.
 #include "common.cuh"
 #include "hotpath.h"
 
@@ -40,8 +38,8 @@ constexpr float RESCALE_THRESHOLD = 8.f;                      // lazy O rescale,
 
 constexpr int STAGES3 = 3;       // K/V tile ring depth
 constexpr int MAX_DECODE_T = DECODE_ROWS / GROUP;             // largest decode / verify batch (10)
-template <bool PRECISE> struct FaLayout {
-    static constexpr int QROWS = PRECISE ? 64 : 128;          // logical query rows per CTA
+struct FaLayout {
+    static constexpr int QROWS = 64;                          // logical query rows per CTA
     static constexpr int SM_KV = 0;                           // ring of (K tile, V tile)
     static constexpr int SM_KV_STAGE = 2 * TILE_BYTES;
     static constexpr int SM_P = SM_KV + STAGES3 * SM_KV_STAGE; // 2 x [128 A-rows][64 pos] fp16
@@ -49,7 +47,7 @@ template <bool PRECISE> struct FaLayout {
     static constexpr int SM_ROPE = SM_BAR + 256;              // decode: (cos, sin) [T][32]
     static constexpr int SMEM_BYTES = SM_ROPE + MAX_DECODE_T * 32 * 8;
 };
-static_assert(FaLayout<true>::SMEM_BYTES <= 227 * 1024, "attention kernel exceeds the shared memory of a CTA");
+static_assert(FaLayout::SMEM_BYTES <= 227 * 1024, "attention kernel exceeds the shared memory of a CTA");
 
 // Rotary inverse frequencies 1e7^(-i/32), i = 0..31, as exact doubles (the
 // values Python's 10000000 ** (-i / 32) yields).
@@ -109,7 +107,7 @@ enum DecodeTail : int {
 
 struct FaParams {
     const __half *q;        // prepared queries [T][24][256] (fp16 of q)
-    const __half *q_lo;     // fp16 of (q - fp16(q)) (PRECISE)
+    const __half *q_lo;     // fp16 of (q - fp16(q))
     const float *q_gate;    // [T][24][512], gate = [256:512), may be null (core prefill)
     float *out;             // [T][24][256]
     float *lse;             // natural-log LSE [T][24] (prefill: optional; decode: TAIL_SHARD)
@@ -442,13 +440,12 @@ __device__ void decode_tail(const FaParams &p, int g, uint8_t *scratch, float *b
     if (threadIdx.x == 0) QV_STAMP(8);
 }
 
-template <bool PRECISE>
-__global__ void __launch_bounds__(PRECISE ? 256 : 384, 1)
+__global__ void __launch_bounds__(256, 1)
 fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
           const FaParams p) {
-    using L = FaLayout<PRECISE>;
+    using L = FaLayout;
     constexpr int QROWS = L::QROWS;
-    constexpr int SOFT_WARPS = PRECISE ? 4 : 8;                // softmax warps
+    constexpr int SOFT_WARPS = 4;                              // softmax warps
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023) {           // 128B-swizzle atoms need a 1024-byte aligned base
         if (threadIdx.x == 0) raise_status(STATUS_BAD_ARGUMENT);
@@ -458,8 +455,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::SM_BAR);
     uint64_t *k_full = bars, *v_full = bars + 3, *k_empty = bars + 6, *v_empty = bars + 9,
              *s_full = bars + 12, *s_free = bars + 14, *p_full = bars + 16, *p_free = bars + 18,
-             *mma_done = bars + 20, *q_ready = bars + 21, *app_done = bars + 22, *xbar = bars + 23,
-             *lbar = bars + 25, *cbar = bars + 26;
+             *mma_done = bars + 20, *q_ready = bars + 21, *app_done = bars + 22, *cbar = bars + 23;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::SM_BAR + 224);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::SM_BAR + 228);
     float2 *rope = reinterpret_cast<float2 *>(smem + L::SM_ROPE);
@@ -493,7 +489,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     // query rows (the q half of q_gate), so that their HBM latency overlaps
     // the previous kernel's tail.  (Prefetching K/V tiles as well measured
     // slower: the extra traffic delays the query loads and thrashes L2.)
-    if (PRECISE && p.fused) {
+    if (p.fused) {
         for (int i = threadIdx.x; i < p.T * GROUP * 8; i += blockDim.x) {    // 8 lines of 128 B per row
             const int rr = i >> 3;
             prefetch_l2(p.q_gate + ((size_t)(rr / GROUP) * NQ + kv_head * GROUP + rr % GROUP) * 2 * HD + (i & 7) * 32);
@@ -508,11 +504,9 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         for (int i = 0; i < 2; ++i) {
             mbar_init(s_full + i, 1); mbar_init(s_free + i, SOFT_WARPS);
             mbar_init(p_full + i, SOFT_WARPS); mbar_init(p_free + i, 1);
-            mbar_init(xbar + i, SOFT_WARPS);
         }
         mbar_init(mma_done, 1);
         mbar_init(q_ready, p.fused ? 8 : 4);      // every warp (fused) or softmax warps 4-7
-        mbar_init(lbar, 4);
         mbar_init(cbar, 1);
         mbar_init(app_done, 64);
         *abort_flag = 0;
@@ -525,15 +519,13 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // Softmax warps 4-7 (and 8-11 in FAST): thread = TMEM lane = A row of the
-    // QK MMA.  FAST: A row = query row; warpgroup wg (warps 4-7 / 8-11) takes
-    // columns [32 wg, 32 wg + 32) of every S tile.  PRECISE: lanes i and i+16
-    // of warp w carry the hi and lo halves of query row 16w+i (one M=128 MMA
-    // yields both).
-    const int wq = (warp - 4) & 3, wg = PRECISE ? 0 : ((warp - 4) >> 2);
+    // Softmax warps 4-7: thread = TMEM lane = A row of the QK MMA; lanes i and
+    // i+16 of warp w carry the hi and lo halves of query row 16w+i (one M=128
+    // MMA yields both).
+    const int wq = (warp - 4) & 3;
     const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
-    const int half = PRECISE ? (lane >> 4) : 0;
-    const int r = PRECISE ? wq * 16 + (lane & 15) : wq * 32 + lane;     // logical query row
+    const int half = lane >> 4;
+    const int r = wq * 16 + (lane & 15);                                // logical query row
     int t = 0, h = 0;
     const bool valid = warp >= 4 && row_token_head<QROWS>(p, r, t, h);
 
@@ -546,7 +538,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     // them on the way into the SM); once warp 0's rows have arrived, tiles
     // 0..2 (all three stages) go out, unless they hold new rows, which must be
     // written first, and the preparation overlaps their loads.
-    const int early = (PRECISE && p.fused) ? min(ntiles, min(app_tile, STAGES3)) : 0;
+    const int early = p.fused ? min(ntiles, min(app_tile, STAGES3)) : 0;
 #ifndef QV_TILES_FIRST
 #define QV_TILES_FIRST 0
 #endif
@@ -565,7 +557,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     if (threadIdx.x == 0) issue_early(0, first_tiles);
     constexpr int QR = DECODE_ROWS / 8;
     float4 xa[QR], xb[QR], n0, n1;
-    if (PRECISE && p.fused) {
+    if (p.fused) {
 #pragma unroll
         for (int j = 0; j < QR; ++j) {
             const int rr = warp + 8 * j;
@@ -581,7 +573,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         n1 = *reinterpret_cast<const float4 *>(p.qn + 128 + 4 * lane);
     }
 
-    if (PRECISE && p.fused) {
+    if (p.fused) {
         // ---------------------------------------- fused prepare (all warps)
         // Query rows r = warp + 8j: RMSNorm with weight, rotary on dims
         // [0,64), split into fp16 hi + lo (hi: the value truncated to fp16's
@@ -702,7 +694,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         }
     } else if (warp >= 4 && warp < 8) {
         // Stage this lane's prepared query row (256 fp16 = 128 columns) into TMEM.
-        const __half *src = (PRECISE && half) ? p.q_lo : p.q;
+        const __half *src = half ? p.q_lo : p.q;
         const uint4 *row = reinterpret_cast<const uint4 *>(src + ((size_t)t * NQ + h) * HD);
 #pragma unroll 2
         for (int c = 0; c < 8; ++c) {
@@ -759,16 +751,10 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 const uint32_t pa = smem_addr(smem + L::SM_P + b * 128 * 128);
                 const uint32_t vb = smem_addr(smem + L::SM_KV + s * L::SM_KV_STAGE + TILE_BYTES);
 #pragma unroll
-                for (int k = 0; k < BN / 16; ++k) {
-                    if (PRECISE)      // P (hi / lo rows) from shared memory
-                        mma_f16_ss(tmem + TM_O, sw128_desc(pa + k * 32, 16, 1024),
-                                   sw128_desc(vb + k * 16 * 128, BN * 128, 1024), idesc_pv,
-                                   (i > 0 || k > 0) ? 1u : 0u);
-                    else              // P written over its S tile in TMEM (fp16, 2 per column)
-                        mma_f16_ts(tmem + TM_O, tmem + TM_S + b * BN + k * 8,
-                                   sw128_desc(vb + k * 16 * 128, BN * 128, 1024), idesc_pv,
-                                   (i > 0 || k > 0) ? 1u : 0u);
-                }
+                for (int k = 0; k < BN / 16; ++k)     // P (hi / lo rows) from shared memory
+                    mma_f16_ss(tmem + TM_O, sw128_desc(pa + k * 32, 16, 1024),
+                               sw128_desc(vb + k * 16 * 128, BN * 128, 1024), idesc_pv,
+                               (i > 0 || k > 0) ? 1u : 0u);
                 mma_commit(p_free + b);
                 mma_commit(v_empty + s);
                 return true;
@@ -778,12 +764,8 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             for (int j = 0; j < ntiles && ok; ++j) {
                 const int b = j & 1, s = j % STAGES3;
                 if (!mbar_wait(k_full + s, (j / STAGES3) & 1, abort_flag)) { ok = false; break; }
-                // S buffer b is reusable once the softmax has read tile j-2.  FAST:
-                // implied by the p_full wait before PV(j-2) (issued above by this
-                // thread), and tile j-2's P, kept in this buffer, is read by PV(j-2)
-                // before this QK writes it: tcgen05.mma issued by one thread execute
-                // in issue order.
-                if (PRECISE && j >= 2 && !mbar_wait(s_free + b, ((j >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
+                // S buffer b is reusable once the softmax has read tile j-2.
+                if (j >= 2 && !mbar_wait(s_free + b, ((j >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t kb = smem_addr(smem + L::SM_KV + s * L::SM_KV_STAGE);
 #pragma unroll
@@ -804,46 +786,33 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         }
     } else if (warp >= 4) {
         // ------------------------------------------------ softmax + epilogue
-        // Each thread handles 32 columns of its row per tile.  FAST: warpgroup
-        // wg takes columns [32 wg, 32 wg + 32); the two warpgroups agree on the
-        // row maximum through a shared-memory exchange (an mbarrier per S
-        // buffer) and keep separate row sums, added after the last tile.
-        // PRECISE: lane i keeps columns [0,32) and lane i+16 columns [32,64) of
-        // row 16w+i, each summing the hi and lo score halves, and each writes
-        // the hi and lo probabilities of its columns.
+        // Each thread handles 32 columns of its row per tile: lane i keeps
+        // columns [0,32) and lane i+16 columns [32,64) of row 16w+i, each summing
+        // the hi and lo score halves, and each writes the hi and lo
+        // probabilities of its columns.
         constexpr int NC = 32;                                     // columns per thread
-        const int cpart = PRECISE ? half : wg;                     // which 32 columns
-        float *xch = reinterpret_cast<float *>(smem + L::SM_ROPE);  // FAST: [2 buffers][2 wg][128 rows]
+        const int cpart = half;                                    // which 32 columns
         const int pos_limit = valid ? p.position + t - p.kv_begin : -1;   // last visible local row
-        const int arow_hi = PRECISE ? wq * 32 + (lane & 15) : r;         // A rows of P (hi, lo)
+        const int arow_hi = wq * 32 + (lane & 15);                 // A rows of P (hi, lo)
         const int arow_lo = arow_hi + 16;
         float m_use = -INFINITY, l = 0.f;
-        bool ok = true;
         for (int j = 0; j < ntiles; ++j) {
             const int b = j & 1;
-            if (!warp_wait(s_full + b, (j >> 1) & 1, abort_flag)) { ok = false; break; }
+            if (!warp_wait(s_full + b, (j >> 1) & 1, abort_flag)) break;
             if (j == 0 && threadIdx.x == 128) QV_STAMP(4);
             tc_fence_after();
             float x[64];
-            if (PRECISE) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    tmem_ld16(t_lane + TM_S + b * BN + c * 16, *reinterpret_cast<float(*)[16]>(x + c * 16));
-            } else {
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-                    tmem_ld16(t_lane + TM_S + b * BN + wg * 32 + c * 16, *reinterpret_cast<float(*)[16]>(x + c * 16));
-            }
+            for (int c = 0; c < 4; ++c)
+                tmem_ld16(t_lane + TM_S + b * BN + c * 16, *reinterpret_cast<float(*)[16]>(x + c * 16));
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free + b);
-            if (PRECISE) {
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const float recv = __shfl_xor_sync(0xffffffffu, half ? x[c] : x[32 + c], 16);
-                    x[c] = (half ? x[32 + c] : x[c]) + recv;
-                }
+            for (int c = 0; c < 32; ++c) {
+                const float recv = __shfl_xor_sync(0xffffffffu, half ? x[c] : x[32 + c], 16);
+                x[c] = (half ? x[32 + c] : x[c]) + recv;
             }
             const int key0 = (tile0 + j) * BN + cpart * 32;
             const int lim = min(pos_limit, p.kv_rows - 1) - key0;     // columns <= lim are visible
@@ -859,27 +828,18 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             }
             float m_tile = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
                                  fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-            if (PRECISE) {
-                m_tile = fmaxf(m_tile, __shfl_xor_sync(0xffffffffu, m_tile, 16));
-            } else {
-                xch[(b * 2 + wg) * 128 + r] = m_tile;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(xbar + b);
-                if (!warp_wait(xbar + b, (j >> 1) & 1, abort_flag)) { ok = false; break; }
-                m_tile = fmaxf(m_tile, xch[(b * 2 + (wg ^ 1)) * 128 + r]);
-            }
+            m_tile = fmaxf(m_tile, __shfl_xor_sync(0xffffffffu, m_tile, 16));
             m_tile *= SCORE_LOG2;                                  // log2 units (-inf stays -inf)
             float factor = 1.f;
             const bool need = m_tile > m_use + RESCALE_THRESHOLD;
             if (need) { factor = exp2_approx(m_use - m_tile); m_use = m_tile; l *= factor; }
             if (j > 0 && __any_sync(0xffffffffu, need)) {
                 // O already holds tiles < j: wait for PV(j-1), then rescale rows in
-                // TMEM (FAST: each warpgroup its half of the columns).
-                if (!warp_wait(p_free + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+                // TMEM.
+                if (!warp_wait(p_free + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) break;
                 tc_fence_after();
-                constexpr int CH = PRECISE ? HD / 16 : HD / 32;
 #pragma unroll 1
-                for (int c = wg * CH; c < wg * CH + CH; ++c) {
+                for (int c = 0; c < HD / 16; ++c) {
                     float o[16];
                     tmem_ld16(t_lane + TM_O + c * 16, o);
                     tmem_wait_ld();
@@ -890,7 +850,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 tmem_wait_st();
             }
             const float mref = m_use == -INFINITY ? 0.f : m_use;
-            uint32_t hi[NC / 2], lo[PRECISE ? NC / 2 : 1];
+            uint32_t hi[NC / 2], lo[NC / 2];
             float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < NC; c += 2) {
@@ -898,185 +858,115 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
                 const float p1 = exp2_approx(fmaf(x[c + 1], SCORE_LOG2, -mref));
                 const __half2 hp = __floats2half2_rn(p0, p1);
                 hi[c / 2] = *reinterpret_cast<const uint32_t *>(&hp);
-                if (PRECISE) {
-                    const float2 back = __half22float2(hp);
-                    const __half2 lp = __floats2half2_rn(p0 - back.x, p1 - back.y);
-                    lo[c / 2] = *reinterpret_cast<const uint32_t *>(&lp);
-                }
+                const float2 back = __half22float2(hp);
+                const __half2 lp = __floats2half2_rn(p0 - back.x, p1 - back.y);
+                lo[c / 2] = *reinterpret_cast<const uint32_t *>(&lp);
                 sp[(c >> 1) & 3] += p0 + p1;
             }
             l += (sp[0] + sp[1]) + (sp[2] + sp[3]);
-            if (PRECISE) {
-                if (j >= 2 && !warp_wait(p_free + b, ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
-                uint8_t *pbuf = smem + L::SM_P + b * 128 * 128;
+            if (j >= 2 && !warp_wait(p_free + b, ((j - 2) >> 1) & 1, abort_flag)) break;
+            uint8_t *pbuf = smem + L::SM_P + b * 128 * 128;
 #pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    const int unit = cpart * 4 + w;
-                    *reinterpret_cast<uint4 *>(pbuf + arow_hi * 128 + ((unit ^ (arow_hi & 7)) << 4)) =
-                        make_uint4(hi[4 * w], hi[4 * w + 1], hi[4 * w + 2], hi[4 * w + 3]);
-                    *reinterpret_cast<uint4 *>(pbuf + arow_lo * 128 + ((unit ^ (arow_lo & 7)) << 4)) =
-                        make_uint4(lo[4 * w], lo[4 * w + 1], lo[4 * w + 2], lo[4 * w + 3]);
-                }
-                fence_async_shared();
-            } else {
-                // fp16 P of columns [32 wg, 32 wg + 32) into TMEM columns [16 wg, 16 wg + 16)
-                // of this S buffer: S columns both warpgroups have read (they passed
-                // the exchange), and which the QK MMA rewrites only after this
-                // tile's PV (issued earlier by the same thread) has consumed them.
-                tmem_st16(t_lane + TM_S + b * BN + wg * 16, *reinterpret_cast<const float(*)[16]>(hi));
-                tmem_wait_st();
+            for (int w = 0; w < 4; ++w) {
+                const int unit = cpart * 4 + w;
+                *reinterpret_cast<uint4 *>(pbuf + arow_hi * 128 + ((unit ^ (arow_hi & 7)) << 4)) =
+                    make_uint4(hi[4 * w], hi[4 * w + 1], hi[4 * w + 2], hi[4 * w + 3]);
+                *reinterpret_cast<uint4 *>(pbuf + arow_lo * 128 + ((unit ^ (arow_lo & 7)) << 4)) =
+                    make_uint4(lo[4 * w], lo[4 * w + 1], lo[4 * w + 2], lo[4 * w + 3]);
             }
+            fence_async_shared();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + b);
         }
         if (threadIdx.x == 128) QV_STAMP(5);
-        if (PRECISE) {
-            // The row's running max and sum, for the epilogue of all warps
-            // (the rotary table is no longer read: every new row is appended).
-            l += __shfl_xor_sync(0xffffffffu, l, 16);
-            if (half == 0) {
-                float *ml_s = reinterpret_cast<float *>(smem + L::SM_ROPE);
-                ml_s[2 * r] = m_use;
-                ml_s[2 * r + 1] = l;
-            }
-            if (valid && half == 0) {
-                if (p.mode == 1) {
-                    if (p.lse) p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * LN2 : -INFINITY;
-                } else {
-                    const size_t slot = ((size_t)kv_head * DECODE_ROWS + r) * MAXS + blockIdx.x;
-                    p.part_ml[slot * 2] = m_use;
-                    p.part_ml[slot * 2 + 1] = l;
-                }
-            }
-        } else {
-            // Warpgroup 1 hands its row sums to warpgroup 0, which writes the output.
-            float *lx = xch + (ntiles & 1) * 256;     // the exchange buffer no tile still reads
-            if (wg == 1) {
-                lx[r] = l;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(lbar);
-                ok = false;                            // the epilogue is warpgroup 0's
-            } else if (ok && warp_wait(lbar, 0, abort_flag)) {
-                l += lx[r];
-            } else {
-                ok = false;
-            }
+        // The row's running max and sum, for the epilogue of all warps
+        // (the rotary table is no longer read: every new row is appended).
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        if (half == 0) {
+            float *ml_s = reinterpret_cast<float *>(smem + L::SM_ROPE);
+            ml_s[2 * r] = m_use;
+            ml_s[2 * r + 1] = l;
         }
-        // FAST epilogue: the final PV's commit on p_free marks O complete (and
-        // every K/V tile consumed, so the ring is idle).  O leaves through shared
-        // memory: every lane puts its TMEM lane into a padded staging row, then
-        // the warp stores each output row as 512-byte pieces.
-        if (!PRECISE && ok && ntiles > 0 &&
-            warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag)) {
-            tc_fence_after();
-            constexpr int RSTRIDE = HD * 4 + 16;                   // staging row bytes (padded)
-            static_assert(4 * 32 * RSTRIDE <= STAGES3 * L::SM_KV_STAGE, "O staging exceeds the K/V ring");
-            uint8_t *stage = smem + L::SM_KV + wq * 32 * RSTRIDE;
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            if (valid && p.lse) p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * LN2 : -INFINITY;
-            uint8_t *myrow = stage + lane * RSTRIDE;
-#pragma unroll 1
-            for (int c4 = 0; c4 < HD / 64; ++c4) {                 // 64 columns per TMEM round trip
-                float o[4][16];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) tmem_ld16(t_lane + TM_O + c4 * 64 + q * 16, o[q]);
-                tmem_wait_ld();
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-#pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4 *>(myrow + (c4 * 64 + q * 16 + e) * 4) =
-                            make_float4(o[q][e] * inv, o[q][e + 1] * inv, o[q][e + 2] * inv, o[q][e + 3] * inv);
-            }
-            __syncwarp();
-            // The valid logical rows of a CTA are a prefix, so are this warp's.
-            const int row0 = wq * 32;
-            const int nvalid = max(0, min(32, p.T - (int)(gridDim.y - 1 - blockIdx.y) * QROWS - row0));
-#pragma unroll 4
-            for (int i = 0; i < nvalid; ++i) {
-                int tt, hh;
-                row_token_head<QROWS>(p, row0 + i, tt, hh);
-                float *dst = p.out + ((size_t)tt * NQ + hh) * HD;
-#pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    const int col = part * 128 + 4 * lane;
-                    *reinterpret_cast<float4 *>(dst + col) = *reinterpret_cast<const float4 *>(stage + i * RSTRIDE + col * 4);
-                }
+        if (valid && half == 0) {
+            if (p.mode == 1) {
+                if (p.lse) p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * LN2 : -INFINITY;
+            } else {
+                const size_t slot = ((size_t)kv_head * DECODE_ROWS + r) * MAXS + blockIdx.x;
+                p.part_ml[slot * 2] = m_use;
+                p.part_ml[slot * 2 + 1] = l;
             }
         }
     }
-    if (PRECISE) {
-        // ------------------------------------------------ epilogue (all 8 warps)
-        // The final PV's commit on p_free marks O complete (and every K/V tile
-        // consumed, so the ring is idle).  Warps w and w+4 share TMEM lane
-        // quarter w%4 (O_hi of row 16(w%4)+i in lane i, O_lo in lane 16+i) and
-        // take O columns [0,128) (warps 4-7) and [128,256) (warps 0-3): each lane
-        // puts its lane's columns into a padded staging row, then the warp
-        // stores each of its rows, the sum of its hi and lo staging rows, as
-        // 512-byte pieces: decode rows as this split's unnormalised partial,
-        // prefill rows divided by their sum and gated.
-        __syncwarp();                                      // warps 0 and 1: lane 0 is back from its role
-        named_barrier(5, 256);                             // the rows' (max, sum) are in shared memory
-        const bool o_ready = ntiles > 0 &&
-                             warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag);
-        if (o_ready) {
-            tc_fence_after();
-            if (threadIdx.x == 128) QV_STAMP(12);
-            const int chalf = warp < 4 ? 1 : 0;
-            constexpr int RS = 128 * 4 + 16;                       // staging row bytes (padded)
-            static_assert(8 * 32 * RS <= STAGES3 * L::SM_KV_STAGE, "O staging exceeds the K/V ring");
-            uint8_t *stage = smem + L::SM_KV + warp * 32 * RS;
-            uint8_t *myrow = stage + lane * RS;
-            const uint32_t ocol = t_lane + TM_O + chalf * 128;
+    // ------------------------------------------------ epilogue (all 8 warps)
+    // The final PV's commit on p_free marks O complete (and every K/V tile
+    // consumed, so the ring is idle).  Warps w and w+4 share TMEM lane
+    // quarter w%4 (O_hi of row 16(w%4)+i in lane i, O_lo in lane 16+i) and
+    // take O columns [0,128) (warps 4-7) and [128,256) (warps 0-3): each lane
+    // puts its lane's columns into a padded staging row, then the warp
+    // stores each of its rows, the sum of its hi and lo staging rows, as
+    // 512-byte pieces: decode rows as this split's unnormalised partial,
+    // prefill rows divided by their sum and gated.
+    __syncwarp();                                      // warps 0 and 1: lane 0 is back from its role
+    named_barrier(5, 256);                             // the rows' (max, sum) are in shared memory
+    const bool o_ready = ntiles > 0 &&
+                         warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag);
+    if (o_ready) {
+        tc_fence_after();
+        if (threadIdx.x == 128) QV_STAMP(12);
+        const int chalf = warp < 4 ? 1 : 0;
+        constexpr int RS = 128 * 4 + 16;                       // staging row bytes (padded)
+        static_assert(8 * 32 * RS <= STAGES3 * L::SM_KV_STAGE, "O staging exceeds the K/V ring");
+        uint8_t *stage = smem + L::SM_KV + warp * 32 * RS;
+        uint8_t *myrow = stage + lane * RS;
+        const uint32_t ocol = t_lane + TM_O + chalf * 128;
 #pragma unroll
-            for (int c4 = 0; c4 < 2; ++c4) {                       // 64 columns per TMEM round trip
-                float o[4][16];
+        for (int c4 = 0; c4 < 2; ++c4) {                       // 64 columns per TMEM round trip
+            float o[4][16];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) tmem_ld16(ocol + c4 * 64 + q * 16, o[q]);
-                tmem_wait_ld();
+            for (int q = 0; q < 4; ++q) tmem_ld16(ocol + c4 * 64 + q * 16, o[q]);
+            tmem_wait_ld();
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
+            for (int q = 0; q < 4; ++q)
 #pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4 *>(myrow + (c4 * 64 + q * 16 + e) * 4) =
-                            make_float4(o[q][e], o[q][e + 1], o[q][e + 2], o[q][e + 3]);
-            }
-            __syncwarp();
-            if (threadIdx.x == 128) QV_STAMP(13);
-            const float *ml_s = reinterpret_cast<const float *>(smem + L::SM_ROPE);
-            const bool direct = p.mode == 1;                       // prefill: final rows; decode: split partials
-            // The valid logical rows of a CTA are a prefix, so are this warp's.
-            const int row0 = wq * 16;
-            const int nvalid = max(0, min(16, (p.mode == 0 ? p.T * GROUP
-                                                           : p.T - (int)(gridDim.y - 1 - blockIdx.y) * QROWS) - row0));
-            const int col = 4 * lane;
-#pragma unroll 4
-            for (int i = 0; i < nvalid; ++i) {
-                const int rr = row0 + i;
-                int tt, hh;
-                row_token_head<QROWS>(p, rr, tt, hh);
-                float4 v = *reinterpret_cast<const float4 *>(stage + i * RS + col * 4);
-                const float4 w = *reinterpret_cast<const float4 *>(stage + (i + 16) * RS + col * 4);
-                v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-                float *dst;
-                if (direct) {
-                    const float lr = ml_s[2 * rr + 1], inv = lr > 0.f ? 1.f / lr : 0.f;
-                    v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
-                    if (p.q_gate) {
-                        const float4 g = *reinterpret_cast<const float4 *>(
-                            p.q_gate + ((size_t)tt * NQ + hh) * 2 * HD + HD + chalf * 128 + col);
-                        v.x *= sigmoidf_(g.x); v.y *= sigmoidf_(g.y);
-                        v.z *= sigmoidf_(g.z); v.w *= sigmoidf_(g.w);
-                    }
-                    dst = p.out + ((size_t)tt * NQ + hh) * HD;
-                } else {
-                    dst = p.part_o + (((size_t)kv_head * DECODE_ROWS + rr) * p.splits + blockIdx.x) * HD;
-                }
-                *reinterpret_cast<float4 *>(dst + chalf * 128 + col) = v;
-            }
-            if (threadIdx.x == 128) QV_STAMP(6);
+                for (int e = 0; e < 16; e += 4)
+                    *reinterpret_cast<float4 *>(myrow + (c4 * 64 + q * 16 + e) * 4) =
+                        make_float4(o[q][e], o[q][e + 1], o[q][e + 2], o[q][e + 3]);
         }
+        __syncwarp();
+        if (threadIdx.x == 128) QV_STAMP(13);
+        const float *ml_s = reinterpret_cast<const float *>(smem + L::SM_ROPE);
+        const bool direct = p.mode == 1;                       // prefill: final rows; decode: split partials
+        // The valid logical rows of a CTA are a prefix, so are this warp's.
+        const int row0 = wq * 16;
+        const int nvalid = max(0, min(16, (p.mode == 0 ? p.T * GROUP
+                                                       : p.T - (int)(gridDim.y - 1 - blockIdx.y) * QROWS) - row0));
+        const int col = 4 * lane;
+#pragma unroll 4
+        for (int i = 0; i < nvalid; ++i) {
+            const int rr = row0 + i;
+            int tt, hh;
+            row_token_head<QROWS>(p, rr, tt, hh);
+            float4 v = *reinterpret_cast<const float4 *>(stage + i * RS + col * 4);
+            const float4 w = *reinterpret_cast<const float4 *>(stage + (i + 16) * RS + col * 4);
+            v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+            float *dst;
+            if (direct) {
+                const float lr = ml_s[2 * rr + 1], inv = lr > 0.f ? 1.f / lr : 0.f;
+                v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
+                if (p.q_gate) {
+                    const float4 g = *reinterpret_cast<const float4 *>(
+                        p.q_gate + ((size_t)tt * NQ + hh) * 2 * HD + HD + chalf * 128 + col);
+                    v.x *= sigmoidf_(g.x); v.y *= sigmoidf_(g.y);
+                    v.z *= sigmoidf_(g.z); v.w *= sigmoidf_(g.w);
+                }
+                dst = p.out + ((size_t)tt * NQ + hh) * HD;
+            } else {
+                dst = p.part_o + (((size_t)kv_head * DECODE_ROWS + rr) * p.splits + blockIdx.x) * HD;
+            }
+            *reinterpret_cast<float4 *>(dst + chalf * 128 + col) = v;
+        }
+        if (threadIdx.x == 128) QV_STAMP(6);
     }
     tc_fence_before();
     __syncthreads();
@@ -1085,7 +975,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     if (threadIdx.x == 0) QV_STAMP(11);
     // Decode: the split combine of this CTA's share of the KV head's rows
     // (the K/V ring and the P buffers are idle now; the P region is scratch).
-    if (PRECISE && p.mode == 0)
+    if (p.mode == 0)
         decode_tail(p, kv_head, smem + L::SM_P, reinterpret_cast<float *>(smem + L::SM_KV), cbar, abort_flag);
 }
 
@@ -1187,20 +1077,13 @@ CUtensorMap cache_map(const void *base, int rows) {
     return m;
 }
 
-void check_launch(const char *what) {
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
-}
-
 // The shared-memory limit of a kernel is a per-device attribute: set it on
 // every device the process launches on.
 PerDeviceOnce g_configured;
 void configure() {
     g_configured.run([] {
-        if (cudaFuncSetAttribute(fa_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 FaLayout<true>::SMEM_BYTES) != cudaSuccess ||
-            cudaFuncSetAttribute(fa_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 FaLayout<false>::SMEM_BYTES) != cudaSuccess)
+        if (cudaFuncSetAttribute(fa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FaLayout::SMEM_BYTES) !=
+            cudaSuccess)
             throw std::runtime_error("cannot reserve shared memory for the attention kernel");
     });
 }
@@ -1229,9 +1112,8 @@ Split decode_split(int kv_rows) {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 bool decode_regime(int T) { return T * GROUP <= DECODE_ROWS; }
 
-template <bool PRECISE>
 void launch_fa(const CUtensorMap &mk, const CUtensorMap &mv, const FaParams &p, dim3 grid, cudaStream_t st) {
-    const cudaError_t e = launch_chained(fa_kernel<PRECISE>, grid, dim3(PRECISE ? 256 : 384), FaLayout<PRECISE>::SMEM_BYTES, st,
+    const cudaError_t e = launch_chained(fa_kernel, grid, dim3(256), FaLayout::SMEM_BYTES, st,
                                          mk, mv, p);
     if (e != cudaSuccess) throw std::runtime_error(std::string("attention kernel launch: ") + cudaGetErrorString(e));
 }
@@ -1273,7 +1155,7 @@ void launch_decode(float *out, float *lse, __half *kc, __half *vc, const float *
     p.tail = tail; p.peers = peers; p.world = world; p.rank = rank; p.seq = seq;
     p.fused = 1; p.key = key; p.value = value; p.qn = qn; p.kn = kn; p.kc = kc; p.vc = vc;
     p.append_row0 = append ? position - kv_begin : -1; p.eps = eps;
-    launch_fa<true>(mk, mv, p, dim3(sp.splits, NKV), st);
+    launch_fa(mk, mv, p, dim3(sp.splits, NKV), st);
 }
 }  // namespace
 
@@ -1290,7 +1172,7 @@ int attention_max_shard_batch() { return MAX_DECODE_T; }
 // output (shard_lse == nullptr) or a normalised partial + LSE (shard mode).
 // Decode / verify batches (T <= 10) use the split-KV regime (one launch, the
 // split combine in its tail); longer blocks use the prefill regime with 64
-// query rows per CTA after a prepare launch; both are PRECISE.
+// query rows per CTA after a prepare launch.
 void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const float *q_gate,
                    const float *key, const float *value, const float *qn, const float *kn, int T,
                    int position, int kv_begin, int kv_rows, bool append, float eps, void *ws,
@@ -1314,8 +1196,8 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
     p.q = qw; p.q_lo = qw_lo; p.q_gate = q_gate; p.T = T; p.position = position;
     p.kv_begin = kv_begin; p.kv_rows = kv_rows;
     p.mode = 1; p.out = out; p.splits = 1;
-    constexpr int R = FaLayout<true>::QROWS;
-    launch_fa<true>(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
+    constexpr int R = FaLayout::QROWS;
+    launch_fa(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
 }
 
 size_t attention_exchange_bytes(int world) { return ex_bytes(world); }
@@ -1340,22 +1222,6 @@ void attention_merge(float *out, const float *parts, const float *lses, int shar
     const cudaError_t e = launch_chained(attn_merge_kernel, dim3(T * NQ), dim3(256), 0, st, out, parts, lses, shards,
                                          T, q_gate);
     if (e != cudaSuccess) throw std::runtime_error(std::string("attention merge: ") + cudaGetErrorString(e));
-}
-
-// Core-level causal prefill on already-prepared fp16 queries (no norm, RoPE
-// or gate): out [T][24][256] = softmax(q.k/16, causal) v, optional LSE.
-// FAST mode: 128 query rows per CTA, fp16 probabilities.
-void prefill_core(float *out, float *lse, const __half *q, const __half *kc, const __half *vc, int T,
-                  int position, cudaStream_t st) {
-    configure();
-    const int kv_rows = position + T;
-    const CUtensorMap mk = cache_map(kc, kv_rows), mv = cache_map(vc, kv_rows);
-    FaParams p{};
-    p.q = q; p.T = T; p.position = position; p.kv_begin = 0; p.kv_rows = kv_rows;
-    p.mode = 1; p.out = out; p.lse = lse; p.splits = 1;
-    constexpr int R = FaLayout<false>::QROWS;
-    launch_fa<false>(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
-    check_launch("prefill attention");
 }
 
 }  // namespace qv

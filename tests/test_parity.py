@@ -156,7 +156,7 @@ def test_config3_prefill_sampled_rows(hot):
         np.testing.assert_allclose(lse[tile_rows][:, heads], exp_lse, atol=1e-3, rtol=0)
 
 
-@pytest.mark.parametrize('L,position', [(1000, 0), (200, 77)])
+@pytest.mark.parametrize('L,position', [(1000, 0), (200, 77), (1, 0), (129, 5), (64, 3000)])
 def test_prefill_core_full(hot, L, position):
     q, k, v = I.prefill_attention(length=L + position, seed=1200 + L)
     q = q[position:]
