@@ -6,6 +6,8 @@
 // library's device error word and returns false, so no kernel can spin
 // forever on a barrier that is never completed.
 #pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -348,6 +350,20 @@ __device__ __forceinline__ float silu_fast(float x) { return x * sigmoid_fast(x)
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 
 // ---------------------------------------------------------------- host set-up
+// cuTensorMapEncodeTiled from the driver, looked up once per process.
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        cudaDriverEntryPointQueryResult q;
+        void *ptr = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !ptr)
+            throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }();
+    return fn;
+}
+
+
 // Runs a set-up step once per CUDA device, with that device current.  Kernel
 // attributes such as the dynamic shared-memory limit are kept per device by
 // the runtime, so a process that drives several GPUs must set them on each;

@@ -2,26 +2,33 @@
 // with W in the GGUF block formats the reference model uses (src/kernels.cu:31-273,
 // 506-552; kinds 8 = Q8_0, 12 = Q4_K, 14 = Q6_K).
 //
-// Design (HBM-bound GEMV with a small batch):
-//  * a CTA of 8 warps owns 32 consecutive rows, 4 per warp; every activation
-//    value a lane loads from shared memory serves the warp's 4 rows;
-//  * the columns are processed in chunks of 256: the activations of a chunk
-//    are staged in shared memory token-major (conflict-free, coalesced), and
-//    the chunk's block bytes of the CTA's 32 rows are staged next to them with
-//    coalesced, independent 16-bit loads (every block size and row length is
-//    even, so 2-byte alignment is all the formats guarantee), unrolled so
-//    that many loads are in flight per thread;
-//  * lane l then takes 4 consecutive columns of a 32-column group (8 lanes
-//    per group, 4 groups per step): one 32-bit load of its quants per row,
-//    the group's scale decoded once for the 4 columns, one 128-bit load of
-//    the activations per token shared by the warp's 4 rows;
-//  * the 4 x 8 per-lane sums are reduced across the warp with a transposing
-//    butterfly (31 shuffles) that leaves sum v on lane v.
-// FAST = true is the reference's dp4a path semantics (runtime.h:17-20): the
-// activations are quantised per 32-column block to 16-bit integers (scale
-// max|x| / 32639, round half away from zero) and the weights' scale part
-// multiplies the quantised activations while the Q4_K minimum part multiplies
-// the exact activations (FP32 scales, sums and accumulation).
+// On the tensor cores (tcgen05, kind::f16, fp32 accumulators in TMEM), HBM-bound:
+//  * A = the integer quants of 128 weight rows (Q8_0: q, Q4_K: the 4-bit q, Q6_K:
+//    q - 32), exact as fp16; the per-row block scales stay out of the MMA;
+//  * B = the activations of 8 tokens as N = 16 columns: per 32-column block x is
+//    scaled by a power of two into [2^14, 2^15) at its maximum and split into
+//    fp16 hi + lo (22 significant bits); the fast variant (the reference's
+//    dp4a-path semantics, runtime.h:17-20) instead quantises x per 32-column
+//    block to 16-bit integers q16 = round(x / s), s = max|x| / 32639, round half
+//    away from zero, split into bytes q16 = 256 hi + lo, so its products are
+//    exact integers;
+//  * one M=128 N=16 K=16 MMA per 16 columns; after every scale group (32
+//    columns, 16 for Q6_K) the accumulator is read back and
+//    acc[t] += (c D_hi + D_lo) * f_tb * s_row - m_row * xsum_tb
+//    (c = 1 or 256, f_tb the block's activation factor, s_row the row's block
+//    scale: Q8_0 d, Q4_K d*sc, Q6_K d*sc; the Q4_K minimum dmin*m times the
+//    block's sum of the exact activations), in fp32.
+// Per CTA of 128 rows, 608 threads:
+//  * warps 16-17: raw GGUF bytes of each 256-column chunk of the 128 rows into a
+//    ring, by asynchronous 8-byte copies (lane = row; a row's later words hit
+//    the L1 lines its first ones brought in), each row's chunk as its
+//    8-byte-aligned superset (the formats only guarantee 2-byte alignment);
+//    their completion is tracked on the ring slot's mbarrier;
+//  * warps 8-15: two threads per row, one per 128-column half of a chunk: quants
+//    to the swizzled fp16 A tile, the row's block scales, and (per half) the B
+//    tile of the 8 tokens with its per-block factors and sums;
+//  * warp 18: MMA issuer, 8 TMEM accumulator slots of 16 columns;
+//  * warps 0-7: readback, thread = (row = TMEM lane, 4 of the 8 tokens).
 #include "common.cuh"
 #include "hotpath.h"
 
@@ -31,164 +38,516 @@
 namespace qv {
 namespace {
 
-constexpr int QM_WARPS = 8, QM_RW = 4, QM_ROWS = QM_WARPS * QM_RW, QM_KC = 256, QM_T = 8;
+constexpr int PM_ROWS = 128;                 // weight rows per CTA (MMA M)
+constexpr int PM_T = 8;                      // tokens
+constexpr int PM_CC = 256;                   // columns per chunk (a K-quant super-block)
+constexpr int PM_HC = 128;                   // columns per stage (half a chunk)
+constexpr int PM_NA = 3;                     // A / B / scale stages
+constexpr int PM_NS = 8;                     // TMEM accumulator slots
+constexpr int PM_THREADS = 608;
+constexpr int PM_A_BYTES = PM_ROWS * PM_HC * 2;      // 32 KB: 2 swizzle atoms of [128 rows][128 B]
+constexpr int PM_B_BYTES = 16 * PM_HC * 2;           // 4 KB: 2 atoms of [16 rows][128 B]
+constexpr int PM_SM_A = 0;
+constexpr int PM_SM_B = PM_SM_A + PM_NA * PM_A_BYTES;
+constexpr int PM_SM_RAW = PM_SM_B + PM_NA * PM_B_BYTES;
+constexpr int PM_RAW_BYTES = 96 * 1024;
+constexpr int PM_SM_SW = PM_SM_RAW + PM_RAW_BYTES;            // [NA][128 rows][8 groups] row scales
+constexpr int PM_SM_MN = PM_SM_SW + PM_NA * PM_ROWS * 8 * 4;  // [NA][128 rows][4 blocks] Q4_K minima
+constexpr int PM_SM_F = PM_SM_MN + PM_NA * PM_ROWS * 4 * 4;   // [NA][8 tokens][4 blocks] activation factors (x 2^24)
+constexpr int PM_SM_XS = PM_SM_F + PM_NA * PM_T * 4 * 4;      // [NA][8 tokens][4 blocks] activation sums
+constexpr int PM_SM_BS = PM_SM_XS + PM_NA * PM_T * 4 * 4;      // [NA][8 tokens][8 groups of 16] quant-bias terms
+constexpr int PM_SM_BAR = PM_SM_BS + PM_NA * PM_T * 8 * 4;
+constexpr int PM_SMEM = PM_SM_BAR + 512;
+static_assert(PM_SMEM <= 227 * 1024, "projection kernel exceeds the shared memory of a CTA");
+static_assert(PM_SM_B % 1024 == 0 && PM_B_BYTES % 1024 == 0 && PM_SM_RAW % 16 == 0, "operand tiles need 1024-byte alignment");
 
-__device__ __forceinline__ float ld_half(const uint8_t *p) {
+template <int KIND> struct PmFormat {
+    static constexpr int SB = KIND == 8 ? 32 : 256;                      // columns per GGUF block
+    static constexpr int BB = KIND == 8 ? 34 : (KIND == 12 ? 144 : 210); // bytes per GGUF block
+    static constexpr int CB = PM_CC / SB * BB;                           // bytes of a full chunk of a row
+    // raw row slot of the copy path: the row's chunk as its 16-byte-aligned
+    // superset (up to 14 bytes before and after an even start); the tensor
+    // path lands rows packed at the chunk's own pitch CB (a multiple of 16)
+    static constexpr int RS_COPY = (CB + 28 + 15) / 16 * 16;
+    static constexpr int G = KIND == 14 ? 16 : 32;                       // columns per scale group
+    static_assert(PM_RAW_BYTES / (PM_ROWS * RS_COPY) >= 2, "raw ring too shallow");
+};
+
+// Byte offset of element `col` (a multiple of 8) of row `row` in a K-major,
+// 128-byte-swizzled operand of `rows` rows: 64-element atoms of rows x 128 B,
+// 16-byte chunks XOR-swizzled by the row's low 3 bits.
+__device__ __forceinline__ uint32_t pm_sw(int rows, int row, int col) {
+    return (uint32_t)((col >> 6) * rows * 128 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4));
+}
+// 32-bit little-endian word at a shared-memory byte address of any alignment.
+__device__ __forceinline__ uint32_t pm_word(const uint8_t *p) {
+    const uint32_t a = smem_addr(p), a0 = a & ~3u;
+    uint32_t w0, w1;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(w0) : "r"(a0));
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(w1) : "r"(a0 + 4));
+    return __funnelshift_r(w0, w1, (a & 3) * 8);
+}
+__device__ __forceinline__ float pm_half(const uint8_t *p) {       // 2-byte aligned fp16
     return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(p)));
+}
+// 32 lanes x 32 bit, 4 consecutive TMEM columns.
+__device__ __forceinline__ void pm_tmem_ld4(uint32_t taddr, float (&v)[4]) {
+    uint32_t r0, r1, r2, r3;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(taddr));
+    v[0] = __uint_as_float(r0); v[1] = __uint_as_float(r1); v[2] = __uint_as_float(r2); v[3] = __uint_as_float(r3);
+}
+__device__ __forceinline__ bool pm_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+}
+
+struct PmArgs {
+    float *out;             // [T][rows]
+    const uint8_t *w;       // rows x row_bytes, 16-byte aligned
+    const float *x;         // [T][width]
+    size_t w_bytes;         // total weight bytes (the end of w)
+    int T, width, rows;
+    int tma;                // 1: rows are 16-byte multiples, chunks arrive by the tensor map
+};
+
+// 3-D tile load global -> shared (16-byte pieces x pieces x rows), completion on
+// the mbarrier's transaction count.
+__device__ __forceinline__ void pm_tma_load_3d(void *dst, const void *tmap, uint64_t *bar, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4, %5}], [%2];"
+                 :: "r"(smem_addr(dst)), "l"(tmap), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z) : "memory");
 }
 
 template <int KIND, bool FAST>
-__global__ void __launch_bounds__(QM_WARPS * 32)
-qmm_kernel(float *out, const uint8_t *w, const float *x, int T, int width, int rows) {
-    constexpr int SB = KIND == 8 ? 32 : 256;                    // columns per block
-    constexpr int BB = KIND == 8 ? 34 : (KIND == 12 ? 144 : 210); // bytes per block
-    constexpr int CB = (QM_KC / SB) * BB;                        // bytes of one row in a full chunk
-    constexpr int CBP = (CB + 15) / 16 * 16;                     // its shared-memory stride (16-byte rows)
-    __shared__ __align__(16) float xs[QM_T][QM_KC];
-    __shared__ __align__(16) float qs[FAST ? QM_T : 1][FAST ? QM_KC : 4];
-    __shared__ __align__(16) uint16_t wbuf[QM_ROWS * CBP / 2];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row0 = blockIdx.x * QM_ROWS + warp * QM_RW;
-    const size_t row_bytes = (size_t)(width / SB) * BB;
+__global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const PmArgs a) {
+    using F = PmFormat<KIND>;
+    constexpr int G = F::G, NGH = PM_HC / G;                            // groups per stage
+    const int RS = a.tma ? F::CB : F::RS_COPY;                          // raw row pitch
+    const int R = min(4, PM_RAW_BYTES / (PM_ROWS * RS));                // raw ring depth
+    extern __shared__ __align__(1024) uint8_t smem[];
+    if (smem_addr(smem) & 1023) {
+        if (threadIdx.x == 0) raise_status(STATUS_BAD_ARGUMENT);
+        return;
+    }
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + PM_SM_BAR);
+    uint64_t *raw_full = bars, *raw_empty = bars + 4, *a_full = bars + 8, *a_empty = bars + 11, *s_empty = bars + 14,
+             *d_full = bars + 17, *d_empty = bars + 25, *mma_done = bars + 33;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PM_SM_BAR + 280);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PM_SM_BAR + 284);
+    float *sw = reinterpret_cast<float *>(smem + PM_SM_SW), *mn = reinterpret_cast<float *>(smem + PM_SM_MN);
+    float *fs = reinterpret_cast<float *>(smem + PM_SM_F), *xs = reinterpret_cast<float *>(smem + PM_SM_XS);
+    float *bs = reinterpret_cast<float *>(smem + PM_SM_BS);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = blockIdx.x * PM_ROWS;
+    const int nrows = min(PM_ROWS, a.rows - row0);
+    const size_t row_bytes = (size_t)(a.width / F::SB) * F::BB;
+    const int nchunks = (a.width + PM_CC - 1) / PM_CC;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < R; ++i) { mbar_init(raw_full + i, a.tma ? 1 : 64); mbar_init(raw_empty + i, 8); }
+        for (int i = 0; i < PM_NA; ++i) { mbar_init(a_full + i, 4); mbar_init(a_empty + i, 1); mbar_init(s_empty + i, 8); }
+        for (int i = 0; i < PM_NS; ++i) { mbar_init(d_full + i, 1); mbar_init(d_empty + i, 8); }
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 18) { tmem_alloc(tmem_slot, PM_NS * 16); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
     grid_dependency_wait();
-    if (tid == 0) launch_dependents();
+    if (threadIdx.x == 0) launch_dependents();
 
-    float acc[QM_RW][QM_T];
-#pragma unroll
-    for (int r = 0; r < QM_RW; ++r)
-#pragma unroll
-        for (int t = 0; t < QM_T; ++t) acc[r][t] = 0.f;
+    // groups of stage u (chunk u / 2, half u % 2); only a partial last Q8_0 chunk has fewer
+    auto stage_groups = [&](int u) {
+        const int len = min(PM_CC, a.width - (u >> 1) * PM_CC) - (u & 1) * PM_HC;
+        return len <= 0 ? 0 : min(NGH, len / G);
+    };
+    const int nstages = 2 * nchunks;
 
-    for (int k0 = 0; k0 < width; k0 += QM_KC) {
-        const int len = min(QM_KC, width - k0);                  // a multiple of 32
-        __syncthreads();                                         // the previous chunk is consumed
-#pragma unroll
-        for (int t = 0; t < QM_T; ++t)
-            for (int kk = tid; kk < len; kk += QM_WARPS * 32)
-                xs[t][kk] = t < T ? x[(size_t)t * width + k0 + kk] : 0.f;
-        {
-            // the chunk's 16-bit words of the CTA's rows; divisions by the
-            // compile-time row stride, a partial last chunk (Q8_0 only) masked
-            constexpr int HW = CB / 2;
-            const int half_words = (len / SB) * BB / 2;
-            const size_t col_off = (size_t)(k0 / SB) * BB;
-            const uint8_t *rows0 = w + (size_t)blockIdx.x * QM_ROWS * row_bytes + col_off;
-            const int nrows = min(QM_ROWS, rows - (int)blockIdx.x * QM_ROWS);
-#pragma unroll 4
-            for (int i = tid; i < QM_ROWS * HW; i += QM_WARPS * 32) {
-                const int r = i / HW, j = i - r * HW;
-                wbuf[r * (CBP / 2) + j] = (r < nrows && j < half_words)
-                              ? reinterpret_cast<const uint16_t *>(rows0 + (size_t)r * row_bytes)[j] : 0;
+    if (warp == 16 || warp == 17) {
+        // ------------------------------------------------ raw bytes producers
+        const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w), wend = wbase + a.w_bytes;
+        if (a.tma) {
+            // one tensor load per chunk: pieces [c CB/16, (c+1) CB/16) of the 128
+            // rows (rows past the matrix read as zeros)
+            if (warp == 16 && lane == 0) {
+                prefetch_tmap(&tmW);
+                int issued = 0;
+                for (int c = 0; c < nchunks; ++c) {
+                    const int slot = c % R;
+                    if (c >= R && !mbar_wait(raw_empty + slot, ((c / R) - 1) & 1, abort_flag)) break;
+                    mbar_expect_tx(raw_full + slot, PM_ROWS * F::CB);
+                    pm_tma_load_3d(smem + PM_SM_RAW + slot * PM_ROWS * RS, &tmW, raw_full + slot, 0, c * (F::CB / 16), row0);
+                    issued = c + 1;
+                }
+                const long long t0 = clock64();
+                for (int c = max(0, issued - R); c < issued; ++c)
+                    while (!mbar_try_wait(raw_full + c % R, (c / R) & 1) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
             }
-        }
-        if (FAST) {
-            __syncthreads();
-            // 16-bit block quantisation of the activations: one warp per (token, 32-block)
-            for (int b = warp; b < QM_T * (len / 32); b += QM_WARPS) {
-                const int t = b / (len / 32), kk = (b % (len / 32)) * 32 + lane;
-                const float v = xs[t][kk];
-                float m = fabsf(v);
+        } else {
+            // 16-byte asynchronous copies, half a warp per row (coalesced): lane l
+            // of warp 16 + p copies pieces l % 16 (+ 16) of rows 64 p + 2 i + l / 16
+            for (int c = 0; c < nchunks; ++c) {
+                const int slot = c % R;
+                if (c >= R && !pm_wait_warp(raw_empty + slot, ((c / R) - 1) & 1, abort_flag)) break;
+                const int cb = min(PM_CC, a.width - c * PM_CC) / F::SB * F::BB;
+                uint8_t *dst0 = smem + PM_SM_RAW + slot * PM_ROWS * RS;
+                for (int i = 0; i < 32; ++i) {
+                    const int r = (warp - 16) * 64 + 2 * i + (lane >> 4);
+                    if (r >= nrows) break;
+                    const uintptr_t st = wbase + (size_t)(row0 + r) * row_bytes + (size_t)c * F::CB;
+                    const uintptr_t a0 = st & ~uintptr_t(15), a1 = (st + cb + 15) & ~uintptr_t(15);
 #pragma unroll
-                for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    for (int pc = 0; pc < 2; ++pc) {
+                        const uintptr_t src = a0 + 16 * ((lane & 15) + 16 * pc);
+                        if (src >= a1) continue;
+                        uint8_t *dst = dst0 + r * RS + (src - a0);
+                        if (src + 16 <= wend) {
+                            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_addr(dst)), "l"(src) : "memory");
+                        } else {
+                            // the matrix's last piece, past the end of the buffer: its
+                            // bytes up to the end (the buffer size is even) by plain loads
+                            for (uintptr_t b = src; b < wend; b += 2)
+                                *reinterpret_cast<uint16_t *>(dst + (b - src)) = *reinterpret_cast<const uint16_t *>(b);
+                        }
+                    }
+                }
+                // the slot's mbarrier counts this lane once its copies have landed
+                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_addr(raw_full + slot)) : "memory");
+            }
+            // every issued copy must land before the CTA may exit
+            asm volatile("cp.async.wait_all;" ::: "memory");
+        }
+    } else if (warp == 18) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(128, 16, false, false);
+            int gseq = 0;
+            bool ok = true;
+            for (int u = 0; u < nstages && ok; ++u) {
+                const int st = u % PM_NA;
+                if (!mbar_wait(a_full + st, (u / PM_NA) & 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t ab = smem_addr(smem + PM_SM_A + st * PM_A_BYTES);
+                const uint32_t bb = smem_addr(smem + PM_SM_B + st * PM_B_BYTES);
+                const int ng = stage_groups(u);
+                for (int g = 0; g < ng; ++g, ++gseq) {
+                    const int slot = gseq % PM_NS;
+                    if (gseq >= PM_NS && !mbar_wait(d_empty + slot, ((gseq / PM_NS) - 1) & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < G / 16; ++kk) {
+                        const int k = g * G + kk * 16;                 // column within the stage
+                        mma_f16_ss(tmem + slot * 16, sw128_desc(ab + (k >> 6) * (PM_ROWS * 128) + (k & 63) * 2, 16, 1024),
+                                   sw128_desc(bb + (k >> 6) * (16 * 128) + (k & 63) * 2, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(d_full + slot);
+                }
+                mma_commit(a_empty + st);
+            }
+            mma_commit(mma_done);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(mma_done, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
+        }
+    } else if (warp >= 8 && warp < 16) {
+        // ------------------------------------------------ converters
+        const int h = (warp - 8) >> 2, r = ((warp - 8) & 3) * 32 + lane, ib = r;   // thread index within its half
+        // thread ib's activations: token ib / 16, columns 8 (ib % 16) .. + 8 of
+        // each of its stages, loaded one stage ahead
+        const int t = ib >> 4, kx = 8 * (ib & 15);
+        const float *xrow = a.x + (size_t)t * a.width + h * PM_HC + kx;
+        float4 xn0 = make_float4(0.f, 0.f, 0.f, 0.f), xn1 = xn0;
+        if (t < a.T && kx < stage_groups(h) * G) {
+            xn0 = reinterpret_cast<const float4 *>(xrow)[0];
+            xn1 = reinterpret_cast<const float4 *>(xrow)[1];
+        }
+        bool ok = true;
+        for (int c = 0; c < nchunks && ok; ++c) {
+            const int u = 2 * c + h, st = u % PM_NA;
+            const int ng = stage_groups(u);
+            float xv[8];
+            xv[0] = xn0.x; xv[1] = xn0.y; xv[2] = xn0.z; xv[3] = xn0.w;
+            xv[4] = xn1.x; xv[5] = xn1.y; xv[6] = xn1.z; xv[7] = xn1.w;
+            xn0 = xn1 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c + 1 < nchunks && t < a.T && kx < stage_groups(u + 2) * G) {
+                xn0 = reinterpret_cast<const float4 *>(xrow + (c + 1) * PM_CC)[0];
+                xn1 = reinterpret_cast<const float4 *>(xrow + (c + 1) * PM_CC)[1];
+            }
+            if (u >= PM_NA) {
+                if (!pm_wait_warp(a_empty + st, ((u / PM_NA) - 1) & 1, abort_flag)) { ok = false; break; }
+                if (!pm_wait_warp(s_empty + st, ((u / PM_NA) - 1) & 1, abort_flag)) { ok = false; break; }
+            }
+            float m = 0.f, xsum = 0.f, bsum = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) { m = fmaxf(m, fabsf(xv[e])); xsum += xv[e]; }
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            uint32_t bh[4], bl[4];
+            float fac;
+            if (FAST) {
                 const float scale = m / 32639.f;
-                float q = 0.f;
-                if (scale != 0.f) {
-                    const float ratio = v / scale;
-                    q = copysignf(floorf(fabsf(ratio) + 0.5f), ratio);
+                int qv[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    float q = 0.f;
+                    if (scale != 0.f) {
+                        const float ratio = xv[e] / scale;
+                        q = copysignf(floorf(fabsf(ratio) + 0.5f), ratio);
+                    }
+                    qv[e] = (int)q;
+                    bsum += q;
                 }
-                qs[t][kk] = scale * q;
-            }
-        }
-        __syncthreads();
-        const uint8_t *wb = reinterpret_cast<const uint8_t *>(wbuf);
-        // lane l covers 4 consecutive columns of a 32-column group: group
-        // 4 step + l / 8 of the chunk, columns 4 (l % 8) .. + 3 within it
-        const int lg = lane >> 3, lc = (lane & 7) * 4;
-        for (int step = 0; step * 128 < len; ++step) {
-            const int c = step * 128 + lg * 32 + lc;             // first column (within the chunk)
-            if (c >= len) continue;                              // a partial Q8_0 chunk
-            float4 x4[QM_T], q4[QM_T];
-            float xsum[QM_T];
 #pragma unroll
-            for (int t = 0; t < QM_T; ++t) {
-                x4[t] = *reinterpret_cast<const float4 *>(&xs[t][c]);
-                q4[t] = FAST ? *reinterpret_cast<const float4 *>(&qs[FAST ? t : 0][FAST ? c : 0]) : x4[t];
-                xsum[t] = (x4[t].x + x4[t].y) + (x4[t].z + x4[t].w);
-            }
+                for (int e = 0; e < 8; e += 2) {
+                    const __half2 hh = __floats2half2_rn((float)(qv[e] >> 8), (float)(qv[e + 1] >> 8));
+                    const __half2 ll = __floats2half2_rn((float)(qv[e] & 255), (float)(qv[e + 1] & 255));
+                    bh[e / 2] = *reinterpret_cast<const uint32_t *>(&hh);
+                    bl[e / 2] = *reinterpret_cast<const uint32_t *>(&ll);
+                }
+                fac = scale;
+            } else {
+                // power-of-two scale taking the block maximum into [2^14, 2^15)
+                int ex = m > 0.f ? ((__float_as_int(m) >> 23) & 255) - 127 : 0;
+                ex = min(max(ex, -100), 100);
+                const float sc = __int_as_float((127 + 14 - ex) << 23);
 #pragma unroll
-            for (int r = 0; r < QM_RW; ++r) {
-                if (row0 + r >= rows) continue;
-                const uint8_t *rb = wb + (warp * QM_RW + r) * CBP;
-                float wq[4], off = 0.f;                           // weight e = wq[e] - off
+                for (int e = 0; e < 8; e += 2) {
+                    const float y0 = xv[e] * sc, y1 = xv[e + 1] * sc;
+                    const __half2 hh = __floats2half2_rn(y0, y1);
+                    const float2 back = __half22float2(hh);
+                    const __half2 ll = __floats2half2_rn(y0 - back.x, y1 - back.y);
+                    const float2 lb = __half22float2(ll);
+                    bsum += (back.x + lb.x) + (back.y + lb.y);
+                    bh[e / 2] = *reinterpret_cast<const uint32_t *>(&hh);
+                    bl[e / 2] = *reinterpret_cast<const uint32_t *>(&ll);
+                }
+                fac = __int_as_float((127 - 14 + ex) << 23);
+            }
+            xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+            xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+            bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);          // per 16 columns
+            uint8_t *bt = smem + PM_SM_B + st * PM_B_BYTES;
+            *reinterpret_cast<uint4 *>(bt + pm_sw(16, t, kx)) = make_uint4(bh[0], bh[1], bh[2], bh[3]);
+            *reinterpret_cast<uint4 *>(bt + pm_sw(16, 8 + t, kx)) = make_uint4(bl[0], bl[1], bl[2], bl[3]);
+            // per 32-column block: the factor of 2^24 sum(a b) (a the biased quant);
+            // per 16 columns: the bias term BIAS sum(b) times the factor
+            constexpr float BIAS = KIND == 8 ? 128.f : (KIND == 14 ? 32.f : 0.f);
+            if ((ib & 3) == 0) {
+                const int q = (st * PM_T + t) * 4 + (kx >> 5);
+                fs[q] = t < a.T ? fac * 16777216.f : 0.f;
+                xs[q] = t < a.T ? xsum : 0.f;
+            }
+            if ((ib & 1) == 0) bs[(st * PM_T + t) * 8 + (kx >> 4)] = t < a.T ? BIAS * bsum * fac : 0.f;
+            // ---- this row's quants of the stage into the A tile as fp16
+            //      subnormals (bits = the small integer k: value k 2^-24, exact),
+            //      unsigned (Q8_0: q + 128, Q6_K: q + 32; the readback removes the
+            //      bias through the block sums), and its scales
+            const int slot = c % R;
+            if (!pm_wait_warp(raw_full + slot, (c / R) & 1, abort_flag)) { ok = false; break; }
+            const uintptr_t s0 = reinterpret_cast<uintptr_t>(a.w) + (size_t)(row0 + r) * row_bytes + (size_t)c * F::CB;
+            const uint8_t *p = smem + PM_SM_RAW + slot * PM_ROWS * RS + r * RS + (a.tma ? 0 : (s0 & 15));
+            uint8_t *at = smem + PM_SM_A + st * PM_A_BYTES;
+            float *swr = sw + (st * PM_ROWS + r) * 8;
+            if (r < nrows) {
                 if (KIND == 8) {
-                    const uint8_t *b = rb + (c >> 5) * BB;          // 34-byte block of this group
-                    const float d = ld_half(b);
-                    const uint32_t lo = *reinterpret_cast<const uint16_t *>(b + 2 + lc);
-                    const uint32_t hi = *reinterpret_cast<const uint16_t *>(b + 4 + lc);
-                    const uint32_t q = lo | (hi << 16);
+                    for (int b = 0; b < ng; ++b) {                                 // 32-column blocks of the stage
+                        const uint8_t *blk = p + (h * 4 + b) * 34;
+                        swr[b] = pm_half(blk);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) wq[e] = d * (float)(int8_t)(q >> (8 * e));
+                        for (int q8 = 0; q8 < 4; ++q8) {
+                            const uint32_t w0 = pm_word(blk + 2 + 8 * q8) ^ 0x80808080u;
+                            const uint32_t w1 = pm_word(blk + 6 + 8 * q8) ^ 0x80808080u;
+                            *reinterpret_cast<uint4 *>(at + pm_sw(PM_ROWS, r, b * 32 + 8 * q8)) =
+                                make_uint4(__byte_perm(w0, 0, 0x4140), __byte_perm(w0, 0, 0x4342),
+                                           __byte_perm(w1, 0, 0x4140), __byte_perm(w1, 0, 0x4342));
+                        }
+                    }
                 } else if (KIND == 12) {
-                    // 6-bit scale and minimum of group g from the 12 packed bytes
-                    const int g = c >> 5;                         // group within the 256-column block
-                    const uint8_t *sc = rb + 4;
-                    const int lo6 = g < 4 ? sc[g] : sc[g + 4];
-                    const int hi2s = g < 4 ? 0 : (sc[g - 4] >> 6) << 4;
-                    const int zlo = g < 4 ? sc[g + 4] : (sc[g + 4] >> 4);
-                    const int hi2z = g < 4 ? 0 : (sc[g] >> 6) << 4;
-                    const float s6 = (float)(g < 4 ? (lo6 & 63) : ((lo6 & 15) | hi2s));
-                    const float z6 = (float)(g < 4 ? (zlo & 63) : (zlo | hi2z));
-                    const float ds = ld_half(rb) * s6;
-                    off = ld_half(rb + 2) * z6;
-                    const uint32_t q = *reinterpret_cast<const uint32_t *>(rb + 16 + (g >> 1) * 32 + lc) >> (4 * (g & 1));
+                    const float d = pm_half(p), dmin = pm_half(p + 2);
+                    const uint8_t *sc = p + 4;
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) wq[e] = ds * (float)((q >> (8 * e)) & 15);
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const int j = 4 * h + jj;                                  // sub-block of the super-block
+                        const int s6 = j < 4 ? (sc[j] & 63) : ((sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4));
+                        const int m6 = j < 4 ? (sc[j + 4] & 63) : ((sc[j + 4] >> 4) | ((sc[j] >> 6) << 4));
+                        swr[jj] = d * (float)s6;
+                        mn[(st * PM_ROWS + r) * 4 + jj] = dmin * (float)m6;
+                    }
+                    // the half's 64 quant bytes (16-byte aligned): byte 32 p + l holds
+                    // column l of sub-blocks 2p (low nibble) and 2p + 1 (high)
+                    const uint4 *qv = reinterpret_cast<const uint4 *>(p + 16 + 64 * h);
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        const uint4 q4 = qv[v];
+                        const uint32_t ws[4] = {q4.x, q4.y, q4.z, q4.w};
+                        uint32_t lo[8], hi[8];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const uint32_t t0 = __byte_perm(ws[e], 0, 0x4140), t1 = __byte_perm(ws[e], 0, 0x4342);
+                            lo[2 * e] = t0 & 0x000F000Fu; lo[2 * e + 1] = t1 & 0x000F000Fu;
+                            hi[2 * e] = (t0 >> 4) & 0x000F000Fu; hi[2 * e + 1] = (t1 >> 4) & 0x000F000Fu;
+                        }
+                        const int c0 = (v >> 1) * 64 + (v & 1) * 16;             // sub-block 2p, columns l0..l0+15
+                        *reinterpret_cast<uint4 *>(at + pm_sw(PM_ROWS, r, c0)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4 *>(at + pm_sw(PM_ROWS, r, c0 + 8)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                        *reinterpret_cast<uint4 *>(at + pm_sw(PM_ROWS, r, c0 + 32)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4 *>(at + pm_sw(PM_ROWS, r, c0 + 40)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                    }
                 } else {
-                    const int half = c >> 7, quarter = (c >> 5) & 3;
-                    const uint32_t low = *reinterpret_cast<const uint32_t *>(rb + half * 64 + (quarter & 1) * 32 + lc)
-                                         >> (4 * (quarter >> 1));
-                    const uint32_t high = *reinterpret_cast<const uint32_t *>(rb + 128 + half * 32 + lc) >> (2 * quarter);
-                    const float ds = (float)(int8_t)rb[192 + (c >> 4)] * ld_half(rb + 208);
+                    const float d = pm_half(p + 208);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        wq[e] = (float)((int)(((high >> (8 * e)) & 3) * 16 + ((low >> (8 * e)) & 15)) - 32) * ds;
-                }
+                    for (int g = 0; g < 8; ++g) swr[g] = d * (float)(int8_t)p[192 + 8 * h + g];
+                    const uint8_t *ql = p + 64 * h, *qh = p + 128 + 32 * h;
 #pragma unroll
-                for (int t = 0; t < QM_T; ++t) {
-                    float a = fmaf(-off, xsum[t], acc[r][t]);
-                    a = fmaf(wq[0], q4[t].x, a);
-                    a = fmaf(wq[1], q4[t].y, a);
-                    a = fmaf(wq[2], q4[t].z, a);
-                    acc[r][t] = fmaf(wq[3], q4[t].w, a);
+                    for (int l0 = 0; l0 < 32; l0 += 8) {
+                        uint32_t wa[2], wb[2], wh[2];
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            wa[e] = pm_word(ql + l0 + 4 * e);                      // quarters 0 (low) and 2 (high)
+                            wb[e] = pm_word(ql + 32 + l0 + 4 * e);                 // quarters 1 and 3
+                            wh[e] = pm_word(qh + l0 + 4 * e);
+                        }
+#pragma unroll
+                        for (int qu = 0; qu < 4; ++qu) {
+                            uint32_t v[4];
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const uint32_t lw = ((qu & 1) ? wb[e] : wa[e]) >> (4 * (qu >> 1));
+                                const int sh = 2 * qu;                              // high bits to bits 4-5 of each byte
+                                const uint32_t hw = sh <= 4 ? (wh[e] << (4 - sh)) : (wh[e] >> (sh - 4));
+                                const uint32_t q6 = (lw & 0x0F0F0F0Fu) | (hw & 0x30303030u);
+                                v[2 * e] = __byte_perm(q6, 0, 0x4140);
+                                v[2 * e + 1] = __byte_perm(q6, 0, 0x4342);
+                            }
+                            *reinterpret_cast<uint4 *>(at + pm_sw(PM_ROWS, r, qu * 32 + l0)) = make_uint4(v[0], v[1], v[2], v[3]);
+                        }
+                    }
                 }
             }
+            // generic-proxy writes of A / B -> visible to the tensor core (async proxy)
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) { mbar_arrive(a_full + st); mbar_arrive(raw_empty + slot); }
+        }
+    } else {
+        // ------------------------------------------------ readback: thread = (row, 4 tokens)
+        // D holds 2^-24 sum_k a_k b_k (a the biased integer quant, b the scaled
+        // activations); per token v = (c D_hi + D_lo) F - B is the block's dot
+        // product of the quants with the activations (F = 2^24 times the block's
+        // activation factor, B its bias term), then acc += v s_row (- m_row xsum
+        // for Q4_K); the stages' sums are added compensated (Kahan).
+        const int r = (warp & 3) * 32 + lane, t0 = 4 * (warp >> 2);
+        const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        float acc[4], cmp[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { acc[k] = 0.f; cmp[k] = 0.f; }
+        int gseq = 0;
+        bool ok = true;
+        for (int u = 0; u < nstages && ok; ++u) {
+            const int st = u % PM_NA;
+            if (!pm_wait_warp(a_full + st, (u / PM_NA) & 1, abort_flag)) { ok = false; break; }
+            const int ng = stage_groups(u);
+            const float *swr = sw + (st * PM_ROWS + r) * 8;
+            const float *fst = fs + st * PM_T * 4, *xst = xs + st * PM_T * 4, *bst = bs + st * PM_T * 8;
+            // up to four groups together: their accumulators are read at once, so
+            // one TMEM round trip serves them
+            constexpr int NB = NGH < 4 ? NGH : 4;
+            float part[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int g0 = 0; g0 < ng && ok; g0 += NB) {
+                float dh[NB][4], dl[NB][4];
+#pragma unroll
+                for (int gg = 0; gg < NB; ++gg) {
+                    if (g0 + gg >= ng) break;
+                    const int q = gseq + g0 + gg, slot = q % PM_NS;
+                    if (!pm_wait_warp(d_full + slot, (q / PM_NS) & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    pm_tmem_ld4(t_lane + slot * 16 + t0, dh[gg]);
+                    pm_tmem_ld4(t_lane + slot * 16 + 8 + t0, dl[gg]);
+                }
+                tmem_wait_ld();                                  // also before leaving on a timeout
+                if (!ok) break;
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    for (int gg = 0; gg < NB && g0 + gg < ng; ++gg) mbar_arrive(d_empty + (gseq + g0 + gg) % PM_NS);
+#pragma unroll
+                for (int gg = 0; gg < NB; ++gg) {
+                    const int g = g0 + gg;
+                    if (g >= ng) break;
+                    const int blk = G == 32 ? g : (g >> 1);
+                    const float s = swr[g], mnr = KIND == 12 ? mn[(st * PM_ROWS + r) * 4 + g] : 0.f;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int t = t0 + k;
+                        const float uv = FAST ? fmaf(256.f, dh[gg][k], dl[gg][k]) : dh[gg][k] + dl[gg][k];
+                        float bt = 0.f;
+                        if (KIND != 12) bt = G == 32 ? bst[t * 8 + 2 * g] + bst[t * 8 + 2 * g + 1] : bst[t * 8 + g];
+                        part[k] = fmaf(fmaf(uv, fst[t * 4 + blk], -bt), s, part[k]);
+                        if (KIND == 12) part[k] = fmaf(-mnr, xst[t * 4 + blk], part[k]);
+                    }
+                }
+            }
+            if (!ok) break;
+            gseq += ng;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_empty + st);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {                      // compensated sum over the stages
+                const float y = part[k] - cmp[k], tt = acc[k] + y;
+                cmp[k] = (tt - acc[k]) - y;
+                acc[k] = tt;
+            }
+        }
+        if (ok && r < nrows) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (t0 + k < a.T) a.out[(size_t)(t0 + k) * a.rows + row0 + r] = acc[k];
         }
     }
-    // transposing butterfly: lane l ends with the sum of value l = r * 8 + t
-    float v[QM_RW * QM_T];
-#pragma unroll
-    for (int r = 0; r < QM_RW; ++r)
-#pragma unroll
-        for (int t = 0; t < QM_T; ++t) v[r * QM_T + t] = acc[r][t];
-#pragma unroll
-    for (int half = 16; half >= 1; half >>= 1) {
-        const bool up = (lane & half) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-            const float lo = v[i], hi = v[i + half];
-            v[i] = (up ? hi : lo) + __shfl_xor_sync(0xffffffffu, up ? lo : hi, half);
-        }
-    }
-    const int r = lane / QM_T, t = lane % QM_T, row = row0 + r;
-    if (row < rows && t < T) out[(size_t)t * rows + row] = v[0];
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 18) tmem_dealloc(tmem, PM_NS * 16);
+}
+
+// 3-D map of the weights as 16-byte pieces: (16 bytes, row_bytes / 16 pieces,
+// rows), boxes of one chunk's pieces of 128 rows.
+template <int KIND>
+CUtensorMap weight_map(const PmArgs &a) {
+    using F = PmFormat<KIND>;
+    CUtensorMap m;
+    const size_t row_bytes = (size_t)(a.width / F::SB) * F::BB;
+    cuuint64_t dims[3] = {16, (cuuint64_t)(row_bytes / 16), (cuuint64_t)a.rows};
+    cuuint64_t strides[2] = {16, (cuuint64_t)row_bytes};
+    cuuint32_t box[3] = {16, (cuuint32_t)(F::CB / 16), (cuuint32_t)PM_ROWS};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(a.w), dims, strides,
+                                            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return m;
 }
 
 template <int KIND>
-cudaError_t launch_kind(float *out, const uint8_t *w, const float *x, int T, int width, int rows, bool fast,
-                        cudaStream_t st) {
-    const dim3 grid((rows + QM_ROWS - 1) / QM_ROWS), block(QM_WARPS * 32);
-    return fast ? launch_chained(qmm_kernel<KIND, true>, grid, block, 0, st, out, w, x, T, width, rows)
-                : launch_chained(qmm_kernel<KIND, false>, grid, block, 0, st, out, w, x, T, width, rows);
+cudaError_t launch_kind(PmArgs a, bool fast, cudaStream_t st) {
+    static PerDeviceOnce configured;
+    configured.run([] {
+        if (cudaFuncSetAttribute(qmm_tc_kernel<KIND, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PM_SMEM) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(qmm_tc_kernel<KIND, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PM_SMEM) !=
+                cudaSuccess)
+            throw std::runtime_error("cannot reserve shared memory for the projection kernel");
+    });
+    using F = PmFormat<KIND>;
+    const size_t row_bytes = (size_t)(a.width / F::SB) * F::BB;
+    a.tma = row_bytes % 16 == 0 && F::CB % 16 == 0 && F::CB / 16 <= 256;
+    CUtensorMap m{};
+    if (a.tma) m = weight_map<KIND>(a);
+    const dim3 grid((a.rows + PM_ROWS - 1) / PM_ROWS), block(PM_THREADS);
+    return fast ? launch_chained(qmm_tc_kernel<KIND, true>, grid, block, PM_SMEM, st, m, a)
+                : launch_chained(qmm_tc_kernel<KIND, false>, grid, block, PM_SMEM, st, m, a);
 }
 
 }  // namespace
@@ -200,12 +559,14 @@ size_t projection_weight_bytes(int kind, int width, int rows) {
 
 void projection_run(float *out, const void *weights, const float *x, int kind, int T, int width, int rows,
                     bool fast, cudaStream_t st) {
-    if (T < 1 || T > QM_T) throw std::invalid_argument("projection batch must be between 1 and 8");
-    const uint8_t *w = static_cast<const uint8_t *>(weights);
+    if (T < 1 || T > PM_T) throw std::invalid_argument("projection batch must be between 1 and 8");
+    if (reinterpret_cast<uintptr_t>(weights) & 15) throw std::invalid_argument("projection weights must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(x) & 15) throw std::invalid_argument("projection activations must be 16-byte aligned");
+    PmArgs a{out, static_cast<const uint8_t *>(weights), x, projection_weight_bytes(kind, width, rows), T, width, rows, 0};
     cudaError_t e;
-    if (kind == 8) e = launch_kind<8>(out, w, x, T, width, rows, fast, st);
-    else if (kind == 12) e = launch_kind<12>(out, w, x, T, width, rows, fast, st);
-    else if (kind == 14) e = launch_kind<14>(out, w, x, T, width, rows, fast, st);
+    if (kind == 8) e = launch_kind<8>(a, fast, st);
+    else if (kind == 12) e = launch_kind<12>(a, fast, st);
+    else if (kind == 14) e = launch_kind<14>(a, fast, st);
     else throw std::invalid_argument("unsupported quantization type");
     if (e != cudaSuccess) throw std::runtime_error(std::string("projection: ") + cudaGetErrorString(e));
 }
