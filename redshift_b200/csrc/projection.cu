@@ -18,7 +18,7 @@
 //    (c = 1 or 256, f_tb the block's activation factor, s_row the row's block
 //    scale: Q8_0 d, Q4_K d*sc, Q6_K d*sc; the Q4_K minimum dmin*m times the
 //    block's sum of the exact activations), in fp32.
-// Per CTA of 128 rows, 608 threads:
+// Per CTA of 128 rows, 640 threads:
 //  * warps 16-17: raw GGUF bytes of each 256-column chunk of the 128 rows into a
 //    ring, by asynchronous 8-byte copies (lane = row; a row's later words hit
 //    the L1 lines its first ones brought in), each row's chunk as its
@@ -27,7 +27,8 @@
 //  * warps 8-15: two threads per row, one per 128-column half of a chunk: quants
 //    to the swizzled fp16 A tile, the row's block scales, and (per half) the B
 //    tile of the 8 tokens with its per-block factors and sums;
-//  * warp 18: MMA issuer, 8 TMEM accumulator slots of 16 columns;
+//  * warps 18-19: MMA issuers (alternate stages), 32 TMEM accumulator slots of
+//    16 columns (8 stages of slack between the MMAs and the readback);
 //  * warps 0-7: readback, thread = (row = TMEM lane, 4 of the 8 tokens).
 #include "common.cuh"
 #include "hotpath.h"
@@ -42,24 +43,30 @@ constexpr int PM_ROWS = 128;                 // weight rows per CTA (MMA M)
 constexpr int PM_T = 8;                      // tokens
 constexpr int PM_CC = 256;                   // columns per chunk (a K-quant super-block)
 constexpr int PM_HC = 128;                   // columns per stage (half a chunk)
-constexpr int PM_NA = 3;                     // A / B / scale stages
-constexpr int PM_NS = 8;                     // TMEM accumulator slots
-constexpr int PM_THREADS = 608;
+constexpr int PM_NS = 32;                    // TMEM accumulator slots (all 512 columns)
+constexpr int PM_THREADS = 640;
 constexpr int PM_A_BYTES = PM_ROWS * PM_HC * 2;      // 32 KB: 2 swizzle atoms of [128 rows][128 B]
 constexpr int PM_B_BYTES = 16 * PM_HC * 2;           // 4 KB: 2 atoms of [16 rows][128 B]
-constexpr int PM_SM_A = 0;
-constexpr int PM_SM_B = PM_SM_A + PM_NA * PM_A_BYTES;
-constexpr int PM_SM_RAW = PM_SM_B + PM_NA * PM_B_BYTES;
-constexpr int PM_RAW_BYTES = 96 * 1024;
-constexpr int PM_SM_SW = PM_SM_RAW + PM_RAW_BYTES;            // [NA][128 rows][8 groups] row scales
-constexpr int PM_SM_MN = PM_SM_SW + PM_NA * PM_ROWS * 8 * 4;  // [NA][128 rows][4 blocks] Q4_K minima
-constexpr int PM_SM_F = PM_SM_MN + PM_NA * PM_ROWS * 4 * 4;   // [NA][8 tokens][4 blocks] activation factors (x 2^24)
-constexpr int PM_SM_XS = PM_SM_F + PM_NA * PM_T * 4 * 4;      // [NA][8 tokens][4 blocks] activation sums
-constexpr int PM_SM_BS = PM_SM_XS + PM_NA * PM_T * 4 * 4;      // [NA][8 tokens][8 groups of 16] quant-bias terms
-constexpr int PM_SM_BAR = PM_SM_BS + PM_NA * PM_T * 8 * 4;
-constexpr int PM_SMEM = PM_SM_BAR + 512;
-static_assert(PM_SMEM <= 227 * 1024, "projection kernel exceeds the shared memory of a CTA");
-static_assert(PM_SM_B % 1024 == 0 && PM_B_BYTES % 1024 == 0 && PM_SM_RAW % 16 == 0, "operand tiles need 1024-byte alignment");
+
+// Shared-memory layout per format: NA stages of A / B / scales and a raw ring.
+// Q4_K (raw chunks by tensor loads, 18 KB each) trades raw-ring depth for a
+// fourth operand stage, which lets the converters run further ahead.
+template <int KIND> struct PmLayout {
+    static constexpr int NA = KIND == 12 ? 4 : 3;
+    static constexpr int NG = KIND == 14 ? 8 : 4;                 // scale groups per stage
+    static constexpr int SM_A = 0;
+    static constexpr int SM_B = SM_A + NA * PM_A_BYTES;
+    static constexpr int SM_SW = SM_B + NA * PM_B_BYTES;          // [NA][128 rows][NG] row scales
+    static constexpr int SM_MN = SM_SW + NA * PM_ROWS * NG * 4;   // [NA][128 rows][4 blocks] Q4_K minima
+    static constexpr int SM_F = SM_MN + NA * PM_ROWS * 4 * 4;     // [NA][8 tokens][4 blocks] activation factors (x 2^24)
+    static constexpr int SM_XS = SM_F + NA * PM_T * 4 * 4;        // [NA][8 tokens][4 blocks] activation sums
+    static constexpr int SM_BS = SM_XS + NA * PM_T * 4 * 4;       // [NA][8 tokens][8 groups of 16] quant-bias terms
+    static constexpr int SM_BAR = SM_BS + NA * PM_T * 8 * 4;
+    static constexpr int SM_RAW = (SM_BAR + 1024 + 127) / 128 * 128;
+    static constexpr int RAW_BYTES = 227 * 1024 - SM_RAW;
+    static constexpr int SMEM = SM_RAW + RAW_BYTES;
+    static_assert(SM_B % 1024 == 0 && PM_B_BYTES % 1024 == 0, "operand tiles need 1024-byte alignment");
+};
 
 template <int KIND> struct PmFormat {
     static constexpr int SB = KIND == 8 ? 32 : 256;                      // columns per GGUF block
@@ -70,7 +77,7 @@ template <int KIND> struct PmFormat {
     // path lands rows packed at the chunk's own pitch CB (a multiple of 16)
     static constexpr int RS_COPY = (CB + 28 + 15) / 16 * 16;
     static constexpr int G = KIND == 14 ? 16 : 32;                       // columns per scale group
-    static_assert(PM_RAW_BYTES / (PM_ROWS * RS_COPY) >= 2, "raw ring too shallow");
+    static_assert(PmLayout<KIND>::RAW_BYTES / (PM_ROWS * RS_COPY) >= 2, "raw ring too shallow");
 };
 
 // Byte offset of element `col` (a multiple of 8) of row `row` in a K-major,
@@ -121,22 +128,24 @@ __device__ __forceinline__ void pm_tma_load_3d(void *dst, const void *tmap, uint
 template <int KIND, bool FAST>
 __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const PmArgs a) {
     using F = PmFormat<KIND>;
-    constexpr int G = F::G, NGH = PM_HC / G;                            // groups per stage
+    using L = PmLayout<KIND>;
+    constexpr int G = F::G, NGH = PM_HC / G, NA = L::NA;               // groups per stage, operand stages
     const int RS = a.tma ? F::CB : F::RS_COPY;                          // raw row pitch
-    const int R = min(4, PM_RAW_BYTES / (PM_ROWS * RS));                // raw ring depth
+    const int R = min(4, L::RAW_BYTES / (PM_ROWS * RS));                // raw ring depth
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023) {
         if (threadIdx.x == 0) raise_status(STATUS_BAD_ARGUMENT);
         return;
     }
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + PM_SM_BAR);
-    uint64_t *raw_full = bars, *raw_empty = bars + 4, *a_full = bars + 8, *a_empty = bars + 11, *s_empty = bars + 14,
-             *d_full = bars + 17, *d_empty = bars + 25, *mma_done = bars + 33;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PM_SM_BAR + 280);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PM_SM_BAR + 284);
-    float *sw = reinterpret_cast<float *>(smem + PM_SM_SW), *mn = reinterpret_cast<float *>(smem + PM_SM_MN);
-    float *fs = reinterpret_cast<float *>(smem + PM_SM_F), *xs = reinterpret_cast<float *>(smem + PM_SM_XS);
-    float *bs = reinterpret_cast<float *>(smem + PM_SM_BS);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::SM_BAR);
+    uint64_t *raw_full = bars, *raw_empty = bars + 4, *a_full = bars + 8, *a_empty = bars + 12, *s_empty = bars + 16,
+             *d_full = bars + 20, *d_empty = d_full + PM_NS, *mma_done = d_empty + PM_NS;     // mma_done: one per issuer
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    static_assert((20 + 2 * PM_NS + 2) * 8 + 8 <= 1024 && NA <= 4, "mbarriers exceed their region");
+    float *sw = reinterpret_cast<float *>(smem + L::SM_SW), *mn = reinterpret_cast<float *>(smem + L::SM_MN);
+    float *fs = reinterpret_cast<float *>(smem + L::SM_F), *xs = reinterpret_cast<float *>(smem + L::SM_XS);
+    float *bs = reinterpret_cast<float *>(smem + L::SM_BS);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * PM_ROWS;
     const int nrows = min(PM_ROWS, a.rows - row0);
@@ -145,9 +154,10 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < R; ++i) { mbar_init(raw_full + i, a.tma ? 1 : 64); mbar_init(raw_empty + i, 8); }
-        for (int i = 0; i < PM_NA; ++i) { mbar_init(a_full + i, 4); mbar_init(a_empty + i, 1); mbar_init(s_empty + i, 8); }
+        for (int i = 0; i < NA; ++i) { mbar_init(a_full + i, 4); mbar_init(a_empty + i, 1); mbar_init(s_empty + i, 8); }
         for (int i = 0; i < PM_NS; ++i) { mbar_init(d_full + i, 1); mbar_init(d_empty + i, 8); }
         mbar_init(mma_done, 1);
+        mbar_init(mma_done + 1, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -179,7 +189,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
                     const int slot = c % R;
                     if (c >= R && !mbar_wait(raw_empty + slot, ((c / R) - 1) & 1, abort_flag)) break;
                     mbar_expect_tx(raw_full + slot, PM_ROWS * F::CB);
-                    pm_tma_load_3d(smem + PM_SM_RAW + slot * PM_ROWS * RS, &tmW, raw_full + slot, 0, c * (F::CB / 16), row0);
+                    pm_tma_load_3d(smem + L::SM_RAW + slot * PM_ROWS * RS, &tmW, raw_full + slot, 0, c * (F::CB / 16), row0);
                     issued = c + 1;
                 }
                 const long long t0 = clock64();
@@ -193,7 +203,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
                 const int slot = c % R;
                 if (c >= R && !pm_wait_warp(raw_empty + slot, ((c / R) - 1) & 1, abort_flag)) break;
                 const int cb = min(PM_CC, a.width - c * PM_CC) / F::SB * F::BB;
-                uint8_t *dst0 = smem + PM_SM_RAW + slot * PM_ROWS * RS;
+                uint8_t *dst0 = smem + L::SM_RAW + slot * PM_ROWS * RS;
                 for (int i = 0; i < 32; ++i) {
                     const int r = (warp - 16) * 64 + 2 * i + (lane >> 4);
                     if (r >= nrows) break;
@@ -220,36 +230,49 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
             // every issued copy must land before the CTA may exit
             asm volatile("cp.async.wait_all;" ::: "memory");
         }
-    } else if (warp == 18) {
-        // ------------------------------------------------ MMA issuer
+    } else if (warp == 18 || warp == 19) {
+        // ------------------------------------------------ MMA issuers: warp 18 + i
+        // takes the stages u with u % 2 == i (one thread's issue rate is below
+        // the tensor core's at N = 16). The operand descriptors of stage 0 are
+        // formed once; a stage and a K step only move their start-address
+        // field (address >> 4, in the low 14 bits: shared-memory addresses stay
+        // below 2^18, so no carry).
+        const int issuer = warp - 18;
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16(128, 16, false, false);
+            const uint64_t ad0 = sw128_desc(smem_addr(smem + L::SM_A), 16, 1024);
+            const uint64_t bd0 = sw128_desc(smem_addr(smem + L::SM_B), 16, 1024);
             int gseq = 0;
             bool ok = true;
             for (int u = 0; u < nstages && ok; ++u) {
-                const int st = u % PM_NA;
-                if (!mbar_wait(a_full + st, (u / PM_NA) & 1, abort_flag)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t ab = smem_addr(smem + PM_SM_A + st * PM_A_BYTES);
-                const uint32_t bb = smem_addr(smem + PM_SM_B + st * PM_B_BYTES);
+                const int st = u % NA;
                 const int ng = stage_groups(u);
-                for (int g = 0; g < ng; ++g, ++gseq) {
-                    const int slot = gseq % PM_NS;
-                    if (gseq >= PM_NS && !mbar_wait(d_empty + slot, ((gseq / PM_NS) - 1) & 1, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
+                if ((u & 1) != issuer) { gseq += ng; continue; }
+                if (!mbar_wait(a_full + st, (u / NA) & 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint64_t ad = ad0 + (uint64_t)(st * PM_A_BYTES >> 4), bd = bd0 + (uint64_t)(st * PM_B_BYTES >> 4);
+#pragma unroll
+                for (int g = 0; g < NGH; ++g) {
+                    if (g >= ng) break;
+                    const int q = gseq + g, slot = q % PM_NS;
+                    if (q >= PM_NS) {
+                        if (!mbar_wait(d_empty + slot, ((q / PM_NS) - 1) & 1, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                    }
 #pragma unroll
                     for (int kk = 0; kk < G / 16; ++kk) {
-                        const int k = g * G + kk * 16;                 // column within the stage
-                        mma_f16_ss(tmem + slot * 16, sw128_desc(ab + (k >> 6) * (PM_ROWS * 128) + (k & 63) * 2, 16, 1024),
-                                   sw128_desc(bb + (k >> 6) * (16 * 128) + (k & 63) * 2, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+                        const int k = g * G + kk * 16;                  // column within the stage (compile-time)
+                        mma_f16_ss(tmem + slot * 16, ad + (uint64_t)(((k >> 6) * (PM_ROWS * 128) + (k & 63) * 2) >> 4),
+                                   bd + (uint64_t)(((k >> 6) * (16 * 128) + (k & 63) * 2) >> 4), idesc, kk > 0 ? 1u : 0u);
                     }
                     mma_commit(d_full + slot);
                 }
+                gseq += ng;
                 mma_commit(a_empty + st);
             }
-            mma_commit(mma_done);
+            mma_commit(mma_done + issuer);
             const long long t0 = clock64();
-            while (!mbar_try_wait(mma_done, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
+            while (!mbar_try_wait(mma_done + issuer, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
         }
     } else if (warp >= 8 && warp < 16) {
         // ------------------------------------------------ converters
@@ -265,7 +288,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
         }
         bool ok = true;
         for (int c = 0; c < nchunks && ok; ++c) {
-            const int u = 2 * c + h, st = u % PM_NA;
+            const int u = 2 * c + h, st = u % NA;
             const int ng = stage_groups(u);
             float xv[8];
             xv[0] = xn0.x; xv[1] = xn0.y; xv[2] = xn0.z; xv[3] = xn0.w;
@@ -275,9 +298,9 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
                 xn0 = reinterpret_cast<const float4 *>(xrow + (c + 1) * PM_CC)[0];
                 xn1 = reinterpret_cast<const float4 *>(xrow + (c + 1) * PM_CC)[1];
             }
-            if (u >= PM_NA) {
-                if (!pm_wait_warp(a_empty + st, ((u / PM_NA) - 1) & 1, abort_flag)) { ok = false; break; }
-                if (!pm_wait_warp(s_empty + st, ((u / PM_NA) - 1) & 1, abort_flag)) { ok = false; break; }
+            if (u >= NA) {
+                if (!pm_wait_warp(a_empty + st, ((u / NA) - 1) & 1, abort_flag)) { ok = false; break; }
+                if (!pm_wait_warp(s_empty + st, ((u / NA) - 1) & 1, abort_flag)) { ok = false; break; }
             }
             float m = 0.f, xsum = 0.f, bsum = 0.f;
 #pragma unroll
@@ -328,7 +351,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
             xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
             xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
             bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);          // per 16 columns
-            uint8_t *bt = smem + PM_SM_B + st * PM_B_BYTES;
+            uint8_t *bt = smem + L::SM_B + st * PM_B_BYTES;
             *reinterpret_cast<uint4 *>(bt + pm_sw(16, t, kx)) = make_uint4(bh[0], bh[1], bh[2], bh[3]);
             *reinterpret_cast<uint4 *>(bt + pm_sw(16, 8 + t, kx)) = make_uint4(bl[0], bl[1], bl[2], bl[3]);
             // per 32-column block: the factor of 2^24 sum(a b) (a the biased quant);
@@ -347,9 +370,9 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
             const int slot = c % R;
             if (!pm_wait_warp(raw_full + slot, (c / R) & 1, abort_flag)) { ok = false; break; }
             const uintptr_t s0 = reinterpret_cast<uintptr_t>(a.w) + (size_t)(row0 + r) * row_bytes + (size_t)c * F::CB;
-            const uint8_t *p = smem + PM_SM_RAW + slot * PM_ROWS * RS + r * RS + (a.tma ? 0 : (s0 & 15));
-            uint8_t *at = smem + PM_SM_A + st * PM_A_BYTES;
-            float *swr = sw + (st * PM_ROWS + r) * 8;
+            const uint8_t *p = smem + L::SM_RAW + slot * PM_ROWS * RS + r * RS + (a.tma ? 0 : (s0 & 15));
+            uint8_t *at = smem + L::SM_A + st * PM_A_BYTES;
+            float *swr = sw + (st * PM_ROWS + r) * L::NG;
             if (r < nrows) {
                 if (KIND == 8) {
                     for (int b = 0; b < ng; ++b) {                                 // 32-column blocks of the stage
@@ -446,10 +469,10 @@ __global__ void __launch_bounds__(PM_THREADS, 1) qmm_tc_kernel(const __grid_cons
         int gseq = 0;
         bool ok = true;
         for (int u = 0; u < nstages && ok; ++u) {
-            const int st = u % PM_NA;
-            if (!pm_wait_warp(a_full + st, (u / PM_NA) & 1, abort_flag)) { ok = false; break; }
+            const int st = u % NA;
+            if (!pm_wait_warp(a_full + st, (u / NA) & 1, abort_flag)) { ok = false; break; }
             const int ng = stage_groups(u);
-            const float *swr = sw + (st * PM_ROWS + r) * 8;
+            const float *swr = sw + (st * PM_ROWS + r) * L::NG;
             const float *fst = fs + st * PM_T * 4, *xst = xs + st * PM_T * 4, *bst = bs + st * PM_T * 8;
             // up to four groups together: their accumulators are read at once, so
             // one TMEM round trip serves them
@@ -534,9 +557,9 @@ template <int KIND>
 cudaError_t launch_kind(PmArgs a, bool fast, cudaStream_t st) {
     static PerDeviceOnce configured;
     configured.run([] {
-        if (cudaFuncSetAttribute(qmm_tc_kernel<KIND, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PM_SMEM) !=
+        if (cudaFuncSetAttribute(qmm_tc_kernel<KIND, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PmLayout<KIND>::SMEM) !=
                 cudaSuccess ||
-            cudaFuncSetAttribute(qmm_tc_kernel<KIND, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PM_SMEM) !=
+            cudaFuncSetAttribute(qmm_tc_kernel<KIND, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PmLayout<KIND>::SMEM) !=
                 cudaSuccess)
             throw std::runtime_error("cannot reserve shared memory for the projection kernel");
     });
@@ -546,8 +569,8 @@ cudaError_t launch_kind(PmArgs a, bool fast, cudaStream_t st) {
     CUtensorMap m{};
     if (a.tma) m = weight_map<KIND>(a);
     const dim3 grid((a.rows + PM_ROWS - 1) / PM_ROWS), block(PM_THREADS);
-    return fast ? launch_chained(qmm_tc_kernel<KIND, true>, grid, block, PM_SMEM, st, m, a)
-                : launch_chained(qmm_tc_kernel<KIND, false>, grid, block, PM_SMEM, st, m, a);
+    return fast ? launch_chained(qmm_tc_kernel<KIND, true>, grid, block, PmLayout<KIND>::SMEM, st, m, a)
+                : launch_chained(qmm_tc_kernel<KIND, false>, grid, block, PmLayout<KIND>::SMEM, st, m, a);
 }
 
 }  // namespace
