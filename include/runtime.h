@@ -132,7 +132,9 @@ int qv_delta(float *out, float *state, float *history,
  * out [batch][rows] = W x for batch 1..8, W [rows][width] in block format
  * `kind` (8 = Q8_0, 12 = Q4_K, 14 = Q6_K; qv_mm_weight_bytes bytes), x
  * [batch][width] f32.  fast != 0 selects the 16-bit activation-block path of
- * qv_test_mm_fast.  All pointers are device memory; asynchronous on `stream`. */
+ * qv_test_mm_fast.  All pointers are device memory; weights and x must be
+ * 16-byte aligned (as cudaMalloc gives; other addresses are rejected).
+ * Asynchronous on `stream`. */
 size_t qv_mm_weight_bytes(int kind, int width, int rows);
 int qv_mm(float *out, const void *weights, const float *x, int kind, int batch,
           int width, int rows, int fast, void *stream);

@@ -124,6 +124,12 @@ def test_device_entry_points_validate_first(lib):
     assert lib.qv_delta_chunked(v, v, v, v, v, v, v, v, v, 64, 16, 48, 32, v, need, None) == -1   # dim 32
     assert lib.qv_delta_chunked(v, v, v, v, v, v, v, v, v, 64, 16, 48, 128, v, need - 1, None) == -1
     assert lib.qv_delta_chunked(v, v, v, v, v, v, v, v, v, 64, 16, 48, 128, None, need, None) == -1
+    # the tensor-core projection streams 16-byte pieces: unaligned weights or activations are rejected
+    a16, odd = ct.c_void_p(4096), ct.c_void_p(4098)
+    assert lib.qv_mm(a16, odd, a16, 12, 8, 512, 7, 0, None) == -1
+    assert b'16-byte aligned' in lib.qv_error()
+    assert lib.qv_mm(a16, a16, odd, 8, 8, 512, 7, 1, None) == -1
+    assert b'16-byte aligned' in lib.qv_error()
 
 
 def _prototype_arg_counts():
