@@ -338,34 +338,52 @@ __device__ void exchange_rows(const FaParams &p, const int (&grow)[2], int nr, f
     auto word_of = [&](int q, int k, int col) {
         return own + (((size_t)slot * world + q) * EX_ROWS + grow[k]) * EX_WORDS + col;
     };
-    const long long t0 = clock64();
-    bool ok = true;
-    auto finish = [&](uint64_t *word, uint64_t x, float fallback) {
-        while ((uint32_t)(x >> 32) != tag32) {
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok = false; return fallback; }
-            x = ld_word_sys(word);
-        }
-        *word = 0;
-        return __uint_as_float((uint32_t)x);
-    };
-    // LSE words: peer q of row k on thread 32k + q
+    // Every word this thread needs (its dimension of the other ranks' rows, and
+    // on threads 32k + q the LSE of rank q's row k) is re-read together until all
+    // carry this call's tag, so the waits for the peers overlap: one round trip
+    // per pass, not one per word.
     const int lk = d >> 5, lq = d & 31;
     const bool lse_reader = lk < nr && lq < world && lq != rank;
-    const uint64_t lse_first = lse_reader ? ld_word_sys(word_of(lq, lk, HD)) : 0;
-    uint64_t first[2][EX_MAX_WORLD];
+    uint64_t w[2][EX_MAX_WORLD], wl = lse_reader ? ld_word_sys(word_of(lq, lk, HD)) : 0;
 #pragma unroll
     for (int k = 0; k < 2; ++k)
 #pragma unroll
         for (int q = 0; q < EX_MAX_WORLD; ++q)
-            first[k][q] = (k < nr && q < world && q != rank) ? ld_word_sys(word_of(q, k, d)) : 0;
-    if (lk < nr && lq < world) sh[lk * EX_MAX_WORLD + lq] = lse_reader ? finish(word_of(lq, lk, HD), lse_first, 0.f) : lse[lk];
+            w[k][q] = (k < nr && q < world && q != rank) ? ld_word_sys(word_of(q, k, d)) : ((uint64_t)tag32 << 32);
+    const long long t0 = clock64();
+    bool ok = true;
+    while (true) {
+        bool ready = !lse_reader || (uint32_t)(wl >> 32) == tag32;
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+            for (int q = 0; q < EX_MAX_WORLD; ++q) ready = ready && (uint32_t)(w[k][q] >> 32) == tag32;
+        if (ready) break;
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_status(STATUS_TIMEOUT); ok = false; break; }
+        if (lse_reader && (uint32_t)(wl >> 32) != tag32) wl = ld_word_sys(word_of(lq, lk, HD));
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+            for (int q = 0; q < EX_MAX_WORLD; ++q)
+                if (k < nr && q < world && q != rank && (uint32_t)(w[k][q] >> 32) != tag32) w[k][q] = ld_word_sys(word_of(q, k, d));
+    }
+    // read words are cleared (a late word of a timed-out call keeps its own tag)
+    if (ok) {
+        if (lse_reader) *word_of(lq, lk, HD) = 0;
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+            for (int q = 0; q < EX_MAX_WORLD; ++q)
+                if (k < nr && q < world && q != rank) *word_of(q, k, d) = 0;
+    }
+    if (lk < nr && lq < world) sh[lk * EX_MAX_WORLD + lq] = lse_reader ? (ok ? __uint_as_float((uint32_t)wl) : 0.f) : lse[lk];
     float val[2][EX_MAX_WORLD];
 #pragma unroll
     for (int k = 0; k < 2; ++k)
 #pragma unroll
         for (int q = 0; q < EX_MAX_WORLD; ++q) {
             val[k][q] = 0.f;
-            if (k < nr && q < world) val[k][q] = q == rank ? o[k] : finish(word_of(q, k, d), first[k][q], 0.f);
+            if (k < nr && q < world) val[k][q] = q == rank ? o[k] : (ok ? __uint_as_float((uint32_t)w[k][q]) : 0.f);
         }
     const int all_ok = __syncthreads_and(ok);
 #pragma unroll

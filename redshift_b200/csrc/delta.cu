@@ -357,6 +357,19 @@ delta_kernel(const DeltaArgs a) {
         }
         __syncthreads();
         if (tid == 0 && chunk == 0) QV_STAMP(5);
+        if (t0 + CHUNK >= a.T) {
+            // the state is final: its store (this CTA's rows only) overlaps the
+            // gated-norm exchange below
+#pragma unroll
+            for (int i = 0; i < NV4; ++i) {
+                if (has_a)
+                    *reinterpret_cast<float4 *>(srow_a + CSTRIDE * i + 4 * j) =
+                        make_float4(Sa[2 * i].x, Sa[2 * i].y, Sa[2 * i + 1].x, Sa[2 * i + 1].y);
+                if (has_b)
+                    *reinterpret_cast<float4 *>(srow_b + CSTRIDE * i + 4 * j) =
+                        make_float4(Sb[2 * i].x, Sb[2 * i].y, Sb[2 * i + 1].x, Sb[2 * i + 1].y);
+            }
+        }
         if (CORE) {
             if (has_out && out_t < n) a.out[((size_t)(t0 + out_t) * Hv + h) * D + row0 + out_i] = O[out_t][out_i];
         } else {
@@ -389,17 +402,10 @@ delta_kernel(const DeltaArgs a) {
         __syncthreads();
     }
 
-#pragma unroll
-    for (int i = 0; i < NV4; ++i) {
-        if (has_a)
-            *reinterpret_cast<float4 *>(srow_a + CSTRIDE * i + 4 * j) =
-                make_float4(Sa[2 * i].x, Sa[2 * i].y, Sa[2 * i + 1].x, Sa[2 * i + 1].y);
-        if (has_b)
-            *reinterpret_cast<float4 *>(srow_b + CSTRIDE * i + 4 * j) =
-                make_float4(Sb[2 * i].x, Sb[2 * i].y, Sb[2 * i + 1].x, Sb[2 * i + 1].y);
-    }
     // History: v channels belong to their rows' CTA; the q/k channels of key
-    // head kh are written by rank 0 of value head kh (h < Hk) only.
+    // head kh are written by rank 0 of value head kh (h < Hk) only, at the end:
+    // the other value heads of key head kh read these channels' old history
+    // after their dependency wait.
     if (!CORE && c >= 0 && (e >= 2 * D || (h < Hk && rank == 0))) {
         a.history[c] = h0; a.history[(size_t)C + c] = h1; a.history[2 * (size_t)C + c] = h2;
     }
