@@ -185,6 +185,51 @@ class Step:
             need = hot.lib.qv_attention_workspace(tokens, self.position)
         self.ws = torch.zeros(max(int(need), 256), dtype=torch.uint8, device=self.dev)   # barrier words start at 0
         self.launches_per_step = len(self.attn) + len(self.delta)   # one launch per layer (split combine / exchange in the tail)
+        if not attention_only:
+            self.pack()
+
+    IN_KEYS = {True: ('q_gate', 'key', 'value'), False: ('qkv', 'gate', 'alpha', 'beta')}
+
+    def layers(self):
+        """(is_attention, buffers) of the 64 layers in step order."""
+        ai = di = 0
+        for layer in range(LAYERS):
+            if layer % 4 == 3:
+                yield True, self.attn[ai]
+                ai += 1
+            else:
+                yield False, self.delta[di]
+                di += 1
+
+    def pack(self):
+        """Every layer's inputs, and separately every layer's output, as views of one device
+        buffer in step order (each view 256-byte aligned), so that the end-to-end step moves
+        them host<->device as one copy per group of four layers instead of one per tensor."""
+        torch, align = self.torch, 64
+
+        def build(entries):
+            offs, n = [], 0
+            for d, k in entries:
+                offs.append(n)
+                n += -(-d[k].numel() // align) * align
+            buf = torch.empty(n, device=self.dev, dtype=torch.float32)
+            for (d, k), o in zip(entries, offs):
+                view = buf[o:o + d[k].numel()].view(d[k].shape)
+                view.copy_(d[k])
+                d[k] = view
+            return buf, offs
+
+        ins, outs, first_in = [], [], []
+        for is_attn, d in self.layers():
+            first_in.append(len(ins))
+            ins += [(d, k) for k in self.IN_KEYS[is_attn]]
+            outs.append((d, 'out'))
+        self.in_dev, in_offs = build(ins)
+        self.out_dev, out_offs = build(outs)
+        starts = [in_offs[i] for i in first_in[::4]] + [self.in_dev.numel()]
+        self.in_groups = list(zip(starts[:-1], starts[1:]))
+        starts = out_offs[::4] + [self.out_dev.numel()]
+        self.out_groups = list(zip(starts[:-1], starts[1:]))
 
     def use_peer_exchange(self, dist):
         """Switch the N>1 attention layers to the fused peer-memory exchange."""
@@ -232,64 +277,51 @@ class Step:
 
     # host-side (pinned) copies of the per-step inputs and outputs, for e2e
     def host_mirror(self):
-        """Pinned host copies of every layer's inputs (each rank feeds its own GPU) and of every
-        layer's output (read back by rank 0 only: the outputs are identical on every rank)."""
+        """Pinned host copies of the packed inputs (each rank feeds its own GPU) and outputs (read
+        back by rank 0 only: the outputs are identical on every rank); returns the bytes a step
+        copies each way."""
         torch = self.torch
         self.readback = self.rank == 0
-        self.h_in_attn, self.h_in_delta, self.h_out_attn, self.h_out_delta = [], [], [], []
-        for a in self.attn:
-            self.h_in_attn.append([(a[k], a[k].cpu().pin_memory()) for k in ('q_gate', 'key', 'value')])
-            self.h_out_attn.append((a['out'], torch.empty_like(a['out'], device='cpu').pin_memory()))
-        for d in self.delta:
-            self.h_in_delta.append([(d[k], d[k].cpu().pin_memory()) for k in ('qkv', 'gate', 'alpha', 'beta')])
-            self.h_out_delta.append((d['out'], torch.empty_like(d['out'], device='cpu').pin_memory()))
+        self.in_host = self.in_dev.cpu().pin_memory()
+        self.out_host = torch.empty_like(self.out_dev, device='cpu').pin_memory()
         self.s_in, self.s_out = torch.cuda.Stream(), torch.cuda.Stream()
-        groups = self.h_in_attn + self.h_in_delta
-        h2d = sum(h.numel() * h.element_size() for group in groups for _, h in group)
-        d2h = sum(h.numel() * h.element_size() for _, h in self.h_out_attn + self.h_out_delta)
+        h2d = self.in_dev.numel() * 4
+        d2h = self.out_dev.numel() * 4 if self.readback else 0
         return h2d, d2h
 
     def run_e2e(self):
-        """One step through the public API from pinned host buffers: every layer's
-        inputs are copied host->device on a copy stream in layer order (each layer
-        waits only for its own inputs), and every layer's output is read back on a
-        second copy stream as soon as the layer is done; the step ends when the
-        last read-back has landed."""
+        """One step through the public API from pinned host buffers: the inputs of each group
+        of four layers are copied host->device on a copy stream in layer order (a group's
+        layers wait only for that group's copy), and each group's outputs are read back on a
+        second copy stream as soon as its last layer is done; the step ends when the last
+        read-back has landed."""
         torch = self.torch
         main = torch.cuda.current_stream()
         start = torch.cuda.Event()
         start.record(main)
         self.s_in.wait_event(start)
         self.s_out.wait_event(start)
-        ready, ai, di = [], 0, 0
+        ready = []
         with torch.cuda.stream(self.s_in):
-            for layer in range(LAYERS):
-                if layer % 4 == 3:
-                    group, ai = self.h_in_attn[ai], ai + 1
-                else:
-                    group, di = self.h_in_delta[di], di + 1
-                for dev, host in group:
-                    dev.copy_(host, non_blocking=True)
+            for lo, hi in self.in_groups:
+                self.in_dev[lo:hi].copy_(self.in_host[lo:hi], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(self.s_in)
                 ready.append(ev)
-        ai = di = 0
-        for layer in range(LAYERS):
-            main.wait_event(ready[layer])
-            if layer % 4 == 3:
-                self.attention_layer(self.attn[ai], seq=ai)
-                dev, host = self.h_out_attn[ai]
-                ai += 1
+        for layer, (is_attn, d) in enumerate(self.layers()):
+            if layer % 4 == 0:
+                main.wait_event(ready[layer // 4])
+            if is_attn:
+                self.attention_layer(d, seq=(layer - 3) // 4)
             else:
-                self.delta_layer(self.delta[di])
-                dev, host = self.h_out_delta[di]
-                di += 1
-            if self.readback:
+                self.delta_layer(d)
+            if self.readback and layer % 4 == 3:
                 done = torch.cuda.Event()
                 done.record(main)
                 self.s_out.wait_event(done)
+                lo, hi = self.out_groups[layer // 4]
                 with torch.cuda.stream(self.s_out):
-                    host.copy_(dev, non_blocking=True)
+                    self.out_host[lo:hi].copy_(self.out_dev[lo:hi], non_blocking=True)
         main.wait_stream(self.s_in)
         main.wait_stream(self.s_out)
 
@@ -451,7 +483,8 @@ def bench_b200(args):
         e_ms = max_over_ranks([e0.elapsed_time(e1) / K])[0]
         e2e = {'value': round(e_ms * 1e3, 2), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
                'd2h_bytes_per_step': d2h, 'launch': 'cuda-graph' if e2e_graph is not None else 'eager',
-               'copies': 'every rank copies its own inputs; rank 0 reads back every layer\'s output'}
+               'copies': 'every rank copies its own inputs, rank 0 reads back every layer\'s output, '
+                         'one copy per group of four layers each way'}
 
     # The attention layers back to back (the sequence split's own figure, free of the replicated
     # DeltaNet layers): every rank times its shards; at N > 1 rank 0 also times the same 16 layers

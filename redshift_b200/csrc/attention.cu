@@ -1,17 +1,17 @@
-// Full-attention hot path for sm_100a: prepare (RMSNorm + partial RoPE + fp16
-// KV append), a tcgen05/TMEM FlashAttention kernel that serves both the
-// decode/verify regime (split-KV, all 6 GQA heads x T tokens of one KV head
-// share every K/V tile) and the reference-semantics prefill regime (64 query
-// positions of one head per CTA), and the shard merge kernel.  The core-level
-// causal prefill with fp16 probabilities is prefill.cu.
+// Full-attention hot path for sm_100a: the decode/verify kernel (split-KV, all
+// 6 GQA heads x T tokens of one KV head share every K/V tile, the prepare step
+// of RMSNorm + partial RoPE + fp16 KV append folded in, the split combine or
+// the peer exchange in its tail), the prepare kernel of the prefill regime
+// (whose attention is prefill.cu's precise instantiation), and the shard
+// merge kernel.
 //
 // Semantics follow the reference's attn_prepare / attention / attention_tiled
 // (src/kernels.cu:415-503) and the CPU oracle tests/cpu_reference.py:55-89:
 // scores q.k/16 over cache rows [0, position+t], softmax, P.V, times
 // sigmoid(gate).
 //
-// Precision: 64 query rows per CTA.  Q is split into fp16 hi = fp16(q) and lo = fp16(q - hi) and the
-//    QK MMA's A operand (held in TMEM) interleaves them: A row 32w+i = Q_hi and
+// Precision: 64 logical query rows per CTA.  Q is split into fp16 hi and
+//    lo = fp16(q - hi) and the QK MMA's A operand (held in TMEM) interleaves them: A row 32w+i = Q_hi and
 //    32w+16+i = Q_lo of query row 16w+i, so one M=128 MMA leaves both score
 //    halves of a row in lanes i and i+16 of warp w, which add them while they
 //    split the row's columns.  Every probability p is split the same way; the
@@ -39,7 +39,6 @@ constexpr float RESCALE_THRESHOLD = 8.f;                      // lazy O rescale,
 constexpr int STAGES3 = 3;       // K/V tile ring depth
 constexpr int MAX_DECODE_T = DECODE_ROWS / GROUP;             // largest decode / verify batch (10)
 struct FaLayout {
-    static constexpr int QROWS = 64;                          // logical query rows per CTA
     static constexpr int SM_KV = 0;                           // ring of (K tile, V tile)
     static constexpr int SM_KV_STAGE = 2 * TILE_BYTES;
     static constexpr int SM_P = SM_KV + STAGES3 * SM_KV_STAGE; // 2 x [128 A-rows][64 pos] fp16
@@ -106,44 +105,34 @@ enum DecodeTail : int {
 };
 
 struct FaParams {
-    const __half *q;        // prepared queries [T][24][256] (fp16 of q)
-    const __half *q_lo;     // fp16 of (q - fp16(q))
-    const float *q_gate;    // [T][24][512], gate = [256:512), may be null (core prefill)
+    const float *q_gate;    // [T][24][512]: q = [0:256), gate = [256:512)
     float *out;             // [T][24][256]
-    float *lse;             // natural-log LSE [T][24] (prefill: optional; decode: TAIL_SHARD)
-    float *part_o;          // decode: [4][64 rows][splits][256] unnormalised partial O of every split
-    float *part_ml;         // decode: [4][64 rows][MAXS][2] (running max in log2 units, sum)
-    unsigned long long *sync;  // decode: [4] per-KV-head barrier words (generation : arrivals)
+    float *lse;             // natural-log LSE [T][24] (TAIL_SHARD)
+    float *part_o;          // [4][64 rows][splits][256] unnormalised partial O of every split
+    float *part_ml;         // [4][64 rows][MAXS][2] (running max in log2 units, sum)
+    unsigned long long *sync;  // [4] per-KV-head barrier words (generation : arrivals)
     int T, position;        // tokens and absolute position of token 0
     int kv_begin;           // absolute position of cache row 0
     int kv_rows;            // valid cache rows
-    int mode;               // 0 = decode (GQA-packed rows, split-KV), 1 = prefill (head-major rows)
     int split_tiles, splits;
-    int tail;               // decode: DecodeTail
+    int tail;               // DecodeTail
     const uint64_t *peers;  // TAIL_EXCHANGE: every rank's receive buffer
     int world, rank, seq;
-    // Decode with the prepare step folded in (fused = 1): the CTA normalises
-    // and rotates its own query rows from q_gate and, when its tiles hold the
-    // block's new cache rows, writes their keys / values before loading them.
-    int fused;
+    // The prepare step folded in: the CTA normalises and rotates its own query
+    // rows from q_gate and, when its tiles hold the block's new cache rows,
+    // writes their keys / values before loading them.
     const float *key, *value, *qn, *kn;
     __half *kc, *vc;        // the caches, for the append
     int append_row0;        // local cache row of token 0's key / value, or -1
     float eps;
 };
 
-// Logical query row -> (token, head).  Decode packs the 6 heads of one KV head
-// and the T tokens; prefill takes QROWS consecutive tokens of one head.
-template <int QROWS>
+// Logical query row -> (token, head): the rows of a CTA pack the 6 query heads
+// of its KV head (blockIdx.y) and the T tokens.
 __device__ __forceinline__ bool row_token_head(const FaParams &p, int r, int &t, int &h) {
-    if (p.mode == 0) {
-        t = r / GROUP;
-        h = blockIdx.y * GROUP + r % GROUP;
-        return r < p.T * GROUP;
-    }
-    t = (gridDim.y - 1 - blockIdx.y) * QROWS + r;
-    h = blockIdx.x;
-    return t < p.T;
+    t = r / GROUP;
+    h = blockIdx.y * GROUP + r % GROUP;
+    return r < p.T * GROUP;
 }
 
 // Warp-uniform bounded wait (all lanes agree on the outcome).
@@ -462,7 +451,6 @@ __global__ void __launch_bounds__(256, 1)
 fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
           const FaParams p) {
     using L = FaLayout;
-    constexpr int QROWS = L::QROWS;
     constexpr int SOFT_WARPS = 4;                              // softmax warps
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023) {           // 128B-swizzle atoms need a 1024-byte aligned base
@@ -479,39 +467,28 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     float2 *rope = reinterpret_cast<float2 *>(smem + L::SM_ROPE);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kv_head = p.mode == 0 ? blockIdx.y : blockIdx.x / GROUP;
+    const int kv_head = blockIdx.y;
 
-    // KV tile range of this CTA (tile = 64 cache rows, local numbering).
-    int tile0, ntiles;
-    if (p.mode == 0) {
-        const int total = (p.kv_rows + BN - 1) / BN;
-        tile0 = blockIdx.x * p.split_tiles;
-        ntiles = min(p.split_tiles, total - tile0);
-    } else {
-        const int qtile = gridDim.y - 1 - blockIdx.y;
-        const int last_tok = min(p.T, (qtile + 1) * QROWS) - 1;
-        const int limit = min(p.kv_rows, p.position + last_tok - p.kv_begin + 1);
-        tile0 = 0;
-        ntiles = (limit + BN - 1) / BN;
-    }
-    // Fused decode: the block's new cache rows that fall into this CTA's tiles.
+    // KV tile range of this CTA's split (tile = 64 cache rows, local numbering).
+    const int total = (p.kv_rows + BN - 1) / BN;
+    const int tile0 = blockIdx.x * p.split_tiles;
+    const int ntiles = min(p.split_tiles, total - tile0);
+    // The block's new cache rows that fall into this CTA's tiles.
     int app_lo = 0, app_hi = 0;
-    if (p.fused && p.append_row0 >= 0) {
+    if (p.append_row0 >= 0) {
         app_lo = max(p.append_row0, tile0 * BN);
         app_hi = min(p.append_row0 + p.T, (tile0 + ntiles) * BN);
     }
     const bool appends = app_hi > app_lo;
     const int app_tile = appends ? app_lo / BN - tile0 : ntiles;    // first tile holding a new row
 
-    // Fused decode, before anything else: L2 prefetch hints for this CTA's
-    // query rows (the q half of q_gate), so that their HBM latency overlaps
-    // the previous kernel's tail.  (Prefetching K/V tiles as well measured
-    // slower: the extra traffic delays the query loads and thrashes L2.)
-    if (p.fused) {
-        for (int i = threadIdx.x; i < p.T * GROUP * 8; i += blockDim.x) {    // 8 lines of 128 B per row
-            const int rr = i >> 3;
-            prefetch_l2(p.q_gate + ((size_t)(rr / GROUP) * NQ + kv_head * GROUP + rr % GROUP) * 2 * HD + (i & 7) * 32);
-        }
+    // Before anything else: L2 prefetch hints for this CTA's query rows (the
+    // q half of q_gate), so that their HBM latency overlaps the previous
+    // kernel's tail.  (Prefetching K/V tiles as well measured slower: the
+    // extra traffic delays the query loads and thrashes L2.)
+    for (int i = threadIdx.x; i < p.T * GROUP * 8; i += blockDim.x) {    // 8 lines of 128 B per row
+        const int rr = i >> 3;
+        prefetch_l2(p.q_gate + ((size_t)(rr / GROUP) * NQ + kv_head * GROUP + rr % GROUP) * 2 * HD + (i & 7) * 32);
     }
 
     if (threadIdx.x == 0) {
@@ -524,7 +501,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             mbar_init(p_full + i, SOFT_WARPS); mbar_init(p_free + i, 1);
         }
         mbar_init(mma_done, 1);
-        mbar_init(q_ready, p.fused ? 8 : 4);      // every warp (fused) or softmax warps 4-7
+        mbar_init(q_ready, 8);                     // every warp, once its query rows are in TMEM
         mbar_init(cbar, 1);
         mbar_init(app_done, 64);
         *abort_flag = 0;
@@ -545,22 +522,18 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     const int half = lane >> 4;
     const int r = wq * 16 + (lane & 15);                                // logical query row
     int t = 0, h = 0;
-    const bool valid = warp >= 4 && row_token_head<QROWS>(p, r, t, h);
+    const bool valid = warp >= 4 && row_token_head(p, r, t, h);
 
     // Everything below may read what the previous kernel of the stream wrote.
     grid_dependency_wait();
     if (threadIdx.x == 0) { launch_dependents(); QV_STAMP(1); }
 
-    // Fused decode: the query rows and norm weights are loaded first (from
-    // L2, ahead of the bulk K/V data, which would otherwise queue in front of
-    // them on the way into the SM); once warp 0's rows have arrived, tiles
-    // 0..2 (all three stages) go out, unless they hold new rows, which must be
-    // written first, and the preparation overlaps their loads.
-    const int early = p.fused ? min(ntiles, min(app_tile, STAGES3)) : 0;
-#ifndef QV_TILES_FIRST
-#define QV_TILES_FIRST 0
-#endif
-    const int first_tiles = min(early, QV_TILES_FIRST);      // tiles issued ahead of the query loads
+    // The query rows and norm weights are loaded first (from L2, ahead of the
+    // bulk K/V data, which would otherwise queue in front of them on the way
+    // into the SM); once every warp's rows have arrived, tiles 0..2 (all
+    // three stages) go out, unless they hold new rows, which must be written
+    // first, and the preparation overlaps their loads.
+    const int early = min(ntiles, min(app_tile, STAGES3));
     auto issue_early = [&](int j0, int j1) {
         for (int j = j0; j < j1; ++j) {
             uint8_t *kd = smem + L::SM_KV + j * L::SM_KV_STAGE, *vd = kd + TILE_BYTES;
@@ -572,10 +545,9 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         }
         QV_STAMP(2);
     };
-    if (threadIdx.x == 0) issue_early(0, first_tiles);
     constexpr int QR = DECODE_ROWS / 8;
     float4 xa[QR], xb[QR], n0, n1;
-    if (p.fused) {
+    {
 #pragma unroll
         for (int j = 0; j < QR; ++j) {
             const int rr = warp + 8 * j;
@@ -591,8 +563,8 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         n1 = *reinterpret_cast<const float4 *>(p.qn + 128 + 4 * lane);
     }
 
-    if (p.fused) {
-        // ---------------------------------------- fused prepare (all warps)
+    {
+        // ---------------------------------------- prepare (all warps)
         // Query rows r = warp + 8j: RMSNorm with weight, rotary on dims
         // [0,64), split into fp16 hi + lo (hi: the value truncated to fp16's
         // 11 significant bits, so that lo = x - hi is exact), placed in TMEM
@@ -614,7 +586,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         named_barrier(1, 256);                                    // the rotary table is complete
         // Every warp has its query rows by now (it summed their squares before
         // the barrier), so the K/V tiles no longer queue in front of them.
-        if (threadIdx.x == 0) issue_early(first_tiles, early);
+        if (threadIdx.x == 0) issue_early(0, early);
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
 #pragma unroll
@@ -710,21 +682,6 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             fence_async_global();
             mbar_arrive(app_done);
         }
-    } else if (warp >= 4 && warp < 8) {
-        // Stage this lane's prepared query row (256 fp16 = 128 columns) into TMEM.
-        const __half *src = half ? p.q_lo : p.q;
-        const uint4 *row = reinterpret_cast<const uint4 *>(src + ((size_t)t * NQ + h) * HD);
-#pragma unroll 2
-        for (int c = 0; c < 8; ++c) {
-            uint4 u[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) u[e] = valid ? row[c * 4 + e] : make_uint4(0, 0, 0, 0);
-            tmem_st16(t_lane + TM_Q + c * 16, *reinterpret_cast<const float(*)[16]>(u));
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(q_ready);
     }
 
     if (warp == 0) {
@@ -898,22 +855,12 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
             if (lane == 0) mbar_arrive(p_full + b);
         }
         if (threadIdx.x == 128) QV_STAMP(5);
-        // The row's running max and sum, for the epilogue of all warps
-        // (the rotary table is no longer read: every new row is appended).
+        // The row's running max and sum, for the split combine.
         l += __shfl_xor_sync(0xffffffffu, l, 16);
-        if (half == 0) {
-            float *ml_s = reinterpret_cast<float *>(smem + L::SM_ROPE);
-            ml_s[2 * r] = m_use;
-            ml_s[2 * r + 1] = l;
-        }
         if (valid && half == 0) {
-            if (p.mode == 1) {
-                if (p.lse) p.lse[(size_t)t * NQ + h] = l > 0.f ? (m_use + log2f(l)) * LN2 : -INFINITY;
-            } else {
-                const size_t slot = ((size_t)kv_head * DECODE_ROWS + r) * MAXS + blockIdx.x;
-                p.part_ml[slot * 2] = m_use;
-                p.part_ml[slot * 2 + 1] = l;
-            }
+            const size_t slot = ((size_t)kv_head * DECODE_ROWS + r) * MAXS + blockIdx.x;
+            p.part_ml[slot * 2] = m_use;
+            p.part_ml[slot * 2 + 1] = l;
         }
     }
     // ------------------------------------------------ epilogue (all 8 warps)
@@ -923,10 +870,9 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     // take O columns [0,128) (warps 4-7) and [128,256) (warps 0-3): each lane
     // puts its lane's columns into a padded staging row, then the warp
     // stores each of its rows, the sum of its hi and lo staging rows, as
-    // 512-byte pieces: decode rows as this split's unnormalised partial,
-    // prefill rows divided by their sum and gated.
+    // 512-byte pieces of this split's unnormalised partial.
     __syncwarp();                                      // warps 0 and 1: lane 0 is back from its role
-    named_barrier(5, 256);                             // the rows' (max, sum) are in shared memory
+    named_barrier(5, 256);
     const bool o_ready = ntiles > 0 &&
                          warp_wait(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag);
     if (o_ready) {
@@ -953,35 +899,17 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
         }
         __syncwarp();
         if (threadIdx.x == 128) QV_STAMP(13);
-        const float *ml_s = reinterpret_cast<const float *>(smem + L::SM_ROPE);
-        const bool direct = p.mode == 1;                       // prefill: final rows; decode: split partials
         // The valid logical rows of a CTA are a prefix, so are this warp's.
         const int row0 = wq * 16;
-        const int nvalid = max(0, min(16, (p.mode == 0 ? p.T * GROUP
-                                                       : p.T - (int)(gridDim.y - 1 - blockIdx.y) * QROWS) - row0));
+        const int nvalid = max(0, min(16, p.T * GROUP - row0));
         const int col = 4 * lane;
 #pragma unroll 4
         for (int i = 0; i < nvalid; ++i) {
             const int rr = row0 + i;
-            int tt, hh;
-            row_token_head<QROWS>(p, rr, tt, hh);
             float4 v = *reinterpret_cast<const float4 *>(stage + i * RS + col * 4);
             const float4 w = *reinterpret_cast<const float4 *>(stage + (i + 16) * RS + col * 4);
             v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-            float *dst;
-            if (direct) {
-                const float lr = ml_s[2 * rr + 1], inv = lr > 0.f ? 1.f / lr : 0.f;
-                v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
-                if (p.q_gate) {
-                    const float4 g = *reinterpret_cast<const float4 *>(
-                        p.q_gate + ((size_t)tt * NQ + hh) * 2 * HD + HD + chalf * 128 + col);
-                    v.x *= sigmoidf_(g.x); v.y *= sigmoidf_(g.y);
-                    v.z *= sigmoidf_(g.z); v.w *= sigmoidf_(g.w);
-                }
-                dst = p.out + ((size_t)tt * NQ + hh) * HD;
-            } else {
-                dst = p.part_o + (((size_t)kv_head * DECODE_ROWS + rr) * p.splits + blockIdx.x) * HD;
-            }
+            float *dst = p.part_o + (((size_t)kv_head * DECODE_ROWS + rr) * p.splits + blockIdx.x) * HD;
             *reinterpret_cast<float4 *>(dst + chalf * 128 + col) = v;
         }
         if (threadIdx.x == 128) QV_STAMP(6);
@@ -991,54 +919,83 @@ fa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUten
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, 512);
     if (threadIdx.x == 0) QV_STAMP(11);
-    // Decode: the split combine of this CTA's share of the KV head's rows
-    // (the K/V ring and the P buffers are idle now; the P region is scratch).
-    if (p.mode == 0)
-        decode_tail(p, kv_head, smem + L::SM_P, reinterpret_cast<float *>(smem + L::SM_KV), cbar, abort_flag);
+    // The split combine of this CTA's share of the KV head's rows (the K/V
+    // ring and the P buffers are idle now; the P region is scratch).
+    decode_tail(p, kv_head, smem + L::SM_P, reinterpret_cast<float *>(smem + L::SM_KV), cbar, abort_flag);
 }
 
 // ---------------------------------------------------------------- prepare
-// One block per (head, token): 24 query heads then 4 key heads.  RMSNorm with
+// One block per token, 8 warps; warp w prepares rows w, w+8, w+16 (and w+24)
+// of the token's 28: the 24 query heads, then the 4 key heads.  RMSNorm with
 // weight, rotary embedding on dims [0,64) as pairs (i, i+32) with angle
-// (position+t) * 1e7^(-i/32) evaluated in double precision, queries written
-// as fp16 operand rows, keys/values rounded to fp16 into the cache.  Used by
-// the prefill regime; decode batches fold this step into fa_kernel.
+// (position+t) * 1e7^(-i/32) evaluated in double precision (the token's 32
+// angles once per block), queries written as fp16 hi / lo operand rows,
+// keys / values rounded to fp16 into the cache.  Lane l of a row holds dims
+// [4l,4l+4) and [128+4l,128+4l+4), as in the decode kernel's prepare step.
+// Used by the prefill regime; decode batches fold this step into fa_kernel.
 __global__ void __launch_bounds__(256)
 attn_prepare_kernel(const float *q_gate, const float *key, const float *value, const float *qn,
                     const float *kn, __half *qw, __half *qw_lo, __half *kc, __half *vc, int position,
                     int append_row0, float eps) {
-    const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
-    const bool isq = h < NQ;
-    const int kh = h - NQ;
+    constexpr int ROWS = NQ + NKV, RPW = (ROWS + 7) / 8;          // rows per token, per warp
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ float2 cs[32];
     grid_dependency_wait();
     launch_dependents();
-    const float *src = isq ? q_gate + ((size_t)t * NQ + h) * 2 * HD : key + ((size_t)t * NKV + kh) * HD;
-    __shared__ float row[HD], red[8];
-    const float x = src[i];
-    float ss = warp_sum(x * x);
-    if ((i & 31) == 0) red[i >> 5] = ss;
-    __syncthreads();
-    ss = 0.f;
+    float4 a[RPW], b[RPW];
 #pragma unroll
-    for (int w = 0; w < 8; ++w) ss += red[w];
-    const float inv = rsqrtf(ss / HD + eps);
-    row[i] = x * inv * (isq ? qn : kn)[i];
-    __syncthreads();
-    if (i < 32) {
-        const float2 cs = rope_angle(position + t, i);
-        const float c = cs.x, s = cs.y, a = row[i], b = row[i + 32];
-        row[i] = a * c - b * s;
-        row[i + 32] = a * s + b * c;
+    for (int j = 0; j < RPW; ++j) {
+        const int h = warp + 8 * j;
+        if (h < ROWS) {
+            const float *src = h < NQ ? q_gate + ((size_t)t * NQ + h) * 2 * HD : key + ((size_t)t * NKV + h - NQ) * HD;
+            a[j] = *reinterpret_cast<const float4 *>(src + 4 * lane);
+            b[j] = *reinterpret_cast<const float4 *>(src + 128 + 4 * lane);
+        }
     }
+    if (threadIdx.x < 32) cs[threadIdx.x] = rope_angle(position + t, threadIdx.x);
     __syncthreads();
-    if (isq) {
-        const __half hi = __float2half_rn(row[i]);
-        qw[((size_t)t * NQ + h) * HD + i] = hi;
-        if (qw_lo) qw_lo[((size_t)t * NQ + h) * HD + i] = __float2half_rn(row[i] - __half2float(hi));
-    } else if (append_row0 >= 0) {
-        const size_t o = ((size_t)(append_row0 + t) * NKV + kh) * HD + i;
-        kc[o] = __float2half_rn(row[i]);
-        vc[o] = __float2half_rn(value[((size_t)t * NKV + kh) * HD + i]);
+#pragma unroll
+    for (int j = 0; j < RPW; ++j) {
+        const int h = warp + 8 * j;
+        if (h >= ROWS) continue;
+        const bool isq = h < NQ;
+        const float *nw = isq ? qn : kn;
+        const float4 n0 = *reinterpret_cast<const float4 *>(nw + 4 * lane);
+        const float4 n1 = *reinterpret_cast<const float4 *>(nw + 128 + 4 * lane);
+        const float4 u = a[j], v = b[j];
+        const float ss = warp_sum(u.x * u.x + u.y * u.y + u.z * u.z + u.w * u.w + v.x * v.x + v.y * v.y +
+                                  v.z * v.z + v.w * v.w);
+        const float inv = rsqrtf(ss / HD + eps);
+        float x0[4] = {u.x * inv * n0.x, u.y * inv * n0.y, u.z * inv * n0.z, u.w * inv * n0.w};
+        const float x1[4] = {v.x * inv * n1.x, v.y * inv * n1.y, v.z * inv * n1.z, v.w * inv * n1.w};
+        rope_row(x0, cs, lane, true);
+        if (isq) {
+            __half *hi = qw + ((size_t)t * NQ + h) * HD, *lo = qw_lo + ((size_t)t * NQ + h) * HD;
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+                const float *x = part ? x1 : x0;
+                const __half2 h0 = __floats2half2_rn(x[0], x[1]), h1 = __floats2half2_rn(x[2], x[3]);
+                const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+                *reinterpret_cast<uint2 *>(hi + part * 128 + 4 * lane) = make_uint2(half2_bits(h0), half2_bits(h1));
+                *reinterpret_cast<uint2 *>(lo + part * 128 + 4 * lane) =
+                    make_uint2(half2_bits(__floats2half2_rn(x[0] - f0.x, x[1] - f0.y)),
+                               half2_bits(__floats2half2_rn(x[2] - f1.x, x[3] - f1.y)));
+            }
+        } else if (append_row0 >= 0) {
+            const int kh = h - NQ;
+            const size_t o = ((size_t)(append_row0 + t) * NKV + kh) * HD;
+            const float *vs = value + ((size_t)t * NKV + kh) * HD;
+            const float4 va = *reinterpret_cast<const float4 *>(vs + 4 * lane);
+            const float4 vb = *reinterpret_cast<const float4 *>(vs + 128 + 4 * lane);
+            *reinterpret_cast<uint2 *>(kc + o + 4 * lane) =
+                make_uint2(half2_bits(__floats2half2_rn(x0[0], x0[1])), half2_bits(__floats2half2_rn(x0[2], x0[3])));
+            *reinterpret_cast<uint2 *>(kc + o + 128 + 4 * lane) =
+                make_uint2(half2_bits(__floats2half2_rn(x1[0], x1[1])), half2_bits(__floats2half2_rn(x1[2], x1[3])));
+            *reinterpret_cast<uint2 *>(vc + o + 4 * lane) =
+                make_uint2(half2_bits(__floats2half2_rn(va.x, va.y)), half2_bits(__floats2half2_rn(va.z, va.w)));
+            *reinterpret_cast<uint2 *>(vc + o + 128 + 4 * lane) =
+                make_uint2(half2_bits(__floats2half2_rn(vb.x, vb.y)), half2_bits(__floats2half2_rn(vb.z, vb.w)));
+        }
     }
 }
 
@@ -1168,10 +1125,10 @@ void launch_decode(float *out, float *lse, __half *kc, __half *vc, const float *
     const CUtensorMap mk = cache_map(kc, kv_rows), mv = cache_map(vc, kv_rows);
     FaParams p{};
     p.q_gate = q_gate; p.out = out; p.lse = lse; p.T = T; p.position = position; p.kv_begin = kv_begin;
-    p.kv_rows = kv_rows; p.mode = 0; p.split_tiles = sp.tiles; p.splits = sp.splits;
+    p.kv_rows = kv_rows; p.split_tiles = sp.tiles; p.splits = sp.splits;
     p.part_o = parts.o; p.part_ml = parts.ml; p.sync = parts.sync;
     p.tail = tail; p.peers = peers; p.world = world; p.rank = rank; p.seq = seq;
-    p.fused = 1; p.key = key; p.value = value; p.qn = qn; p.kn = kn; p.kc = kc; p.vc = vc;
+    p.key = key; p.value = value; p.qn = qn; p.kn = kn; p.kc = kc; p.vc = vc;
     p.append_row0 = append ? position - kv_begin : -1; p.eps = eps;
     launch_fa(mk, mv, p, dim3(sp.splits, NKV), st);
 }
@@ -1189,8 +1146,8 @@ int attention_max_shard_batch() { return MAX_DECODE_T; }
 // position - kv_begin when append is true.  Writes either the final gated
 // output (shard_lse == nullptr) or a normalised partial + LSE (shard mode).
 // Decode / verify batches (T <= 10) use the split-KV regime (one launch, the
-// split combine in its tail); longer blocks use the prefill regime with 64
-// query rows per CTA after a prepare launch.
+// split combine in its tail); longer blocks use the prefill regime: a prepare
+// launch, then prefill.cu's precise kernel (128 queries per CTA, 128-key tiles).
 void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const float *q_gate,
                    const float *key, const float *value, const float *qn, const float *kn, int T,
                    int position, int kv_begin, int kv_rows, bool append, float eps, void *ws,
@@ -1206,16 +1163,10 @@ void attention_run(float *out, float *shard_lse, __half *kc, __half *vc, const f
     uint8_t *w = static_cast<uint8_t *>(ws);
     const size_t q_bytes = align256((size_t)T * NQ * HD * sizeof(__half));
     __half *qw = reinterpret_cast<__half *>(w), *qw_lo = reinterpret_cast<__half *>(w + q_bytes);
-    const cudaError_t e = launch_chained(attn_prepare_kernel, dim3(T, NQ + NKV), dim3(256), 0, st, q_gate, key, value,
+    const cudaError_t e = launch_chained(attn_prepare_kernel, dim3(T), dim3(256), 0, st, q_gate, key, value,
                                          qn, kn, qw, qw_lo, kc, vc, position, append ? position - kv_begin : -1, eps);
     if (e != cudaSuccess) throw std::runtime_error(std::string("attention prepare: ") + cudaGetErrorString(e));
-    const CUtensorMap mk = cache_map(kc, kv_rows), mv = cache_map(vc, kv_rows);
-    FaParams p{};
-    p.q = qw; p.q_lo = qw_lo; p.q_gate = q_gate; p.T = T; p.position = position;
-    p.kv_begin = kv_begin; p.kv_rows = kv_rows;
-    p.mode = 1; p.out = out; p.splits = 1;
-    constexpr int R = FaLayout::QROWS;
-    launch_fa(mk, mv, p, dim3(NQ, (T + R - 1) / R), st);
+    prefill_precise(out, qw, qw_lo, q_gate, kc, vc, T, position - kv_begin, kv_rows, st);
 }
 
 size_t attention_exchange_bytes(int world) { return ex_bytes(world); }

@@ -26,6 +26,11 @@ void attention_shard_exchange(float *out, __half *kc, __half *vc, const float *q
                               int world, int rank, int seq, void *ws, size_t ws_bytes, cudaStream_t st);
 void prefill_core(float *out, float *lse, const __half *q, const __half *kc, const __half *vc, int T,
                   int position, cudaStream_t st);
+// Prefill regime of attention_run (prefill.cu): prepared hi / lo query rows,
+// cache rows [0, kv_rows), token t sees rows [0, position + t], output times
+// sigmoid(gate) when q_gate is given.
+void prefill_precise(float *out, const __half *q, const __half *q_lo, const float *q_gate, const __half *kc,
+                     const __half *vc, int T, int position, int kv_rows, cudaStream_t st);
 
 // Gated DeltaNet (delta.cu).
 void delta_run(float *out, float *state, float *history, const float *qkv, const float *gate,

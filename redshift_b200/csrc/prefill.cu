@@ -1,27 +1,41 @@
-// Causal prefill attention core (benchmark configuration 3): already-prepared
-// fp16 queries q [T][24][256] against the fp16 caches [rows][4][256],
-// out [T][24][256] = softmax(q.k / 16 over cache rows [0, position + t]) v,
-// with fp16 probabilities and fp32 accumulation; the semantics of
-// tests/cpu_reference.py:72-88 (scores, softmax, P.V) over a causal block.
+// Causal prefill attention on tcgen05, two instantiations of one kernel:
+//  * prefill_core (benchmark configuration 3): already-prepared fp16 queries
+//    q [T][24][256] against the fp16 caches [rows][4][256],
+//    out [T][24][256] = softmax(q.k / 16 over cache rows [0, position + t]) v,
+//    with fp16 probabilities and fp32 accumulation; the semantics of
+//    tests/cpu_reference.py:72-88 (scores, softmax, P.V) over a causal block.
+//  * prefill_precise (the attention layer's prefill regime, the reference's
+//    attention_tiled, src/kernels.cu:459-503, whose scores and probabilities
+//    are fp32): queries and probabilities are split into fp16 hi = fp16(x) and
+//    lo = fp16(x - hi), and the lo halves extend the MMAs' reduction: the
+//    scores are [Q_hi | Q_lo] . [K | K]^T and the output [P_hi | P_lo] . [V ; V],
+//    the second half of each product issued as separate K=16 steps on the same
+//    shared-memory K or V operand, so the fp32 accumulator of a row holds
+//    (hi + lo) . K and scores and probabilities keep ~22 mantissa bits; the
+//    output is multiplied by sigmoid(gate).
 //
-// One CTA per (128 query rows, query head), 384 threads:
-//  * warp 0: TMA producer. The CTA's 128 queries (64 KB, four 128B-swizzled
-//    boxes) once, then the K and V tiles of 128 keys as 16 KB chunks into a
-//    ring of ten slots, in the order the MMA warp consumes them:
-//    K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1). A K chunk is 128 keys x
-//    64 dims (one box), a V chunk 32 keys x 256 dims (four boxes of 64 dims).
-//  * warp 1: MMA issuer. S_j = Q K_j^T as 16 M=128 N=128 K=16 MMAs into one of
-//    two 128-column TMEM buffers, then O += P_(j-1) V_(j-1) as 8 M=128 N=256
-//    MMAs whose A operand, the fp16 probabilities, is read from TMEM, where
-//    the softmax wrote them over their own score tile. A 128-key tile keeps
-//    the QK instruction at N=128, where tcgen05 runs at its full rate (N=64
-//    issues at about two thirds of it).
+// One CTA per (128 queries, query head), 384 threads:
+//  * warp 0: TMA producer. The CTA's query rows once (64 KB per fp16 half, four
+//    128B-swizzled 64-dim column chunks each), then the K and V tiles of 128
+//    keys as 16 KB chunks into a ring of slots, in the order the MMA warp
+//    consumes them: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1). A K chunk
+//    is 128 keys x 64 dims (one box), a V chunk 32 keys x 256 dims (four boxes
+//    of 64 dims).
+//  * warp 1: MMA issuer. S_j = Q K_j^T as M=128 N=128 K=16 MMAs (16, or 32 in
+//    the precise form) into one of two 128-column TMEM buffers, then
+//    O += P_(j-1) V_(j-1) as M=128 N=256 MMAs (8, or 16) whose A operand, the
+//    fp16 probabilities, is read from TMEM, where the softmax wrote them over
+//    their own score tile. A 128-key tile keeps the QK instruction at N=128,
+//    where tcgen05 runs at its full rate (N=64 issues at about two thirds of
+//    it).
 //  * warps 4-11: softmax, two warpgroups; thread = TMEM lane = query row,
 //    warpgroup g takes keys [64g, 64g+64) of every tile. The row maximum is
-//    agreed through shared memory once per tile, the O rescale is lazy
-//    (only when the maximum grew by more than 2^8), and each warpgroup keeps
-//    its own row sum. Epilogue: warpgroup g writes O columns [128g, 128g+128).
-// TMEM: S buffers [0, 256), O [256, 512). Shared memory: Q 64 KB + ring 160 KB.
+//    agreed through shared memory once per tile, the O rescale is lazy (only
+//    when the maximum grew by more than 2^8), and each warpgroup keeps its own
+//    row sum. Epilogue: warpgroup g writes O columns [128g, 128g+128).
+// TMEM: S buffers [0, 256), O [256, 512). A score buffer's probabilities take
+// its columns [0, 64) (fp16 pairs), the precise form's lo halves [64, 128).
+// Shared memory: Q 64 KB + a ring of ten slots, or Q hi + lo 128 KB + six.
 #include "common.cuh"
 #include "hotpath.h"
 
@@ -34,17 +48,23 @@ namespace qv {
 
 namespace {
 constexpr int PF_NQ = 24, PF_NKV = 4, PF_HD = 256, PF_GROUP = PF_NQ / PF_NKV;
-constexpr int PF_QROWS = 128;                  // query rows per CTA
+constexpr int PF_QROWS = 128;                  // queries per CTA
 constexpr int PF_BN = 128;                     // keys per tile
-constexpr int PF_SLOTS = 10;                   // ring slots
-constexpr int PF_CHUNK = 16384;                // bytes per ring slot
-constexpr int PF_SM_Q = 0;                     // 4 boxes of [128 rows][128 B]
-constexpr int PF_SM_RING = PF_SM_Q + 4 * PF_CHUNK;
-constexpr int PF_SM_XCH = PF_SM_RING + PF_SLOTS * PF_CHUNK;   // [2 buffers][2 warpgroups][128 rows] floats
-constexpr int PF_SM_BAR = PF_SM_XCH + 2 * 2 * 128 * 4;
-constexpr int PF_SMEM_BYTES = PF_SM_BAR + 256;
-static_assert(PF_SMEM_BYTES <= 227 * 1024, "prefill kernel exceeds the shared memory of a CTA");
+constexpr int PF_CHUNK = 16384;                // bytes per ring slot, and per 64-dim query chunk
+template <bool PRECISE>
+struct PfLayout {
+    static constexpr int SLOTS = PRECISE ? 6 : 10;                  // ring slots
+    static constexpr int SM_Q = 0;                                  // 4 chunks of [128 rows][128 B]
+    static constexpr int SM_QLO = SM_Q + 4 * PF_CHUNK;              // precise: the lo halves, 4 chunks
+    static constexpr int SM_RING = SM_Q + (PRECISE ? 8 : 4) * PF_CHUNK;
+    static constexpr int SM_XCH = SM_RING + SLOTS * PF_CHUNK;       // [2 buffers][2 warpgroups][128 rows] floats
+    static constexpr int SM_BAR = SM_XCH + 2 * 2 * 128 * 4;
+    static constexpr int SMEM_BYTES = SM_BAR + 256;
+    static_assert(SMEM_BYTES <= 227 * 1024, "prefill kernel exceeds the shared memory of a CTA");
+    static_assert((2 * SLOTS + 11) * 8 <= 248, "mbarriers overlap the TMEM address slot");
+};
 constexpr uint32_t PF_TM_S = 0, PF_TM_O = 256;
+constexpr uint32_t PF_TM_PLO = 64;             // lo probabilities within a score buffer
 constexpr float PF_SCORE_LOG2 = 0.0625f * 1.4426950408889634f;   // (1/16) * log2(e)
 constexpr float PF_RESCALE_THRESHOLD = 8.f;                      // lazy O rescale, log2 units
 constexpr float PF_LN2 = 0.6931471805599453f;
@@ -52,28 +72,32 @@ constexpr float PF_LN2 = 0.6931471805599453f;
 struct PfParams {
     float *out;          // [T][24][256]
     float *lse;          // [T][24] natural-log LSE, or null
+    const float *q_gate; // [T][24][512], gate = [256:512), or null (no gate)
     int T, position;     // tokens; cache row of token 0
-    int kv_rows;         // position + T
+    int kv_rows;         // valid cache rows (>= position + T)
 };
 
 __device__ __forceinline__ bool warp_wait_all(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
 }
 
+template <bool PRECISE>
 __global__ void __launch_bounds__(384, 1)
-prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-               const __grid_constant__ CUtensorMap tmV, const PfParams p) {
+prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmQlo,
+               const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const PfParams p) {
+    using L = PfLayout<PRECISE>;
+    constexpr int SLOTS = L::SLOTS;
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023) {           // 128B-swizzle atoms need a 1024-byte aligned base
         if (threadIdx.x == 0) raise_status(STATUS_BAD_ARGUMENT);
         return;
     }
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + PF_SM_BAR);
-    uint64_t *full = bars, *empty = bars + PF_SLOTS, *q_full = bars + 2 * PF_SLOTS, *s_full = q_full + 1,
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::SM_BAR);
+    uint64_t *full = bars, *empty = bars + SLOTS, *q_full = bars + 2 * SLOTS, *s_full = q_full + 1,
              *p_full = s_full + 2, *p_free = p_full + 2, *xbar = p_free + 2, *lbar = xbar + 2, *mma_done = lbar + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PF_SM_BAR + 248);      // after the 31 mbarriers
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PF_SM_BAR + 252);
-    float *xch = reinterpret_cast<float *>(smem + PF_SM_XCH);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::SM_BAR + 248);      // after the mbarriers
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::SM_BAR + 252);
+    float *xch = reinterpret_cast<float *>(smem + L::SM_XCH);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int head = blockIdx.x, kv_head = head / PF_GROUP;
@@ -83,7 +107,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const int ntiles = (min(p.kv_rows, p.position + last_tok + 1) + PF_BN - 1) / PF_BN;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < PF_SLOTS; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
+        for (int i = 0; i < SLOTS; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
         mbar_init(q_full, 1);
         for (int i = 0; i < 2; ++i) {
             mbar_init(s_full + i, 1);
@@ -96,7 +120,12 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 0 && lane == 0) { prefetch_tmap(&tmQ); prefetch_tmap(&tmK); prefetch_tmap(&tmV); }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmQ);
+        if (PRECISE) prefetch_tmap(&tmQlo);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+    }
     if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
     tc_fence_before();
     __syncthreads();
@@ -110,9 +139,12 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            mbar_expect_tx(q_full, 4 * PF_CHUNK);
-            for (int c = 0; c < 4; ++c)
-                tma_load_2d(smem + PF_SM_Q + c * PF_CHUNK, &tmQ, q_full, head * PF_HD + c * 64, tok0);
+            mbar_expect_tx(q_full, (PRECISE ? 8 : 4) * PF_CHUNK);
+            for (int c = 0; c < 4; ++c) {
+                tma_load_2d(smem + L::SM_Q + c * PF_CHUNK, &tmQ, q_full, head * PF_HD + c * 64, tok0);
+                if (PRECISE)
+                    tma_load_2d(smem + L::SM_QLO + c * PF_CHUNK, &tmQlo, q_full, head * PF_HD + c * 64, tok0);
+            }
             int seq = 0;
             bool ok = true;
             // Step s of the consumption order: s = 0 -> K0; s = 2i+1 -> K(i+1)
@@ -125,9 +157,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 else if (s & 1) { tile = (s + 1) / 2; is_k = tile < ntiles; if (!is_k) tile = ntiles - 1; }
                 else { is_k = false; tile = s / 2 - 1; }
                 for (int c = 0; c < 4 && ok; ++c, ++seq) {
-                    const int slot = seq % PF_SLOTS;
-                    if (seq >= PF_SLOTS && !mbar_wait(empty + slot, ((seq / PF_SLOTS) - 1) & 1, abort_flag)) { ok = false; break; }
-                    uint8_t *dst = smem + PF_SM_RING + slot * PF_CHUNK;
+                    const int slot = seq % SLOTS;
+                    if (seq >= SLOTS && !mbar_wait(empty + slot, ((seq / SLOTS) - 1) & 1, abort_flag)) { ok = false; break; }
+                    uint8_t *dst = smem + L::SM_RING + slot * PF_CHUNK;
                     mbar_expect_tx(full + slot, PF_CHUNK);
                     if (is_k) {
                         tma_load_2d(dst, &tmK, full + slot, kv_head * PF_HD + c * 64, tile * PF_BN);
@@ -141,19 +173,20 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             // Drain: every issued load must land before the CTA may exit.
             const long long t0 = clock64();
             while (!mbar_try_wait(q_full, 0) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
-            for (int i = max(0, seq - PF_SLOTS); i < seq; ++i)
-                while (!mbar_try_wait(full + i % PF_SLOTS, (i / PF_SLOTS) & 1) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
+            for (int i = max(0, seq - SLOTS); i < seq; ++i)
+                while (!mbar_try_wait(full + i % SLOTS, (i / SLOTS) & 1) && clock64() - t0 < WAIT_LIMIT_CYCLES) {}
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc_qk = idesc_f16(128, PF_BN, false, false);
             constexpr uint32_t idesc_pv = idesc_f16(128, PF_HD, false, true);
-            const uint32_t qa = smem_addr(smem + PF_SM_Q), ring = smem_addr(smem + PF_SM_RING);
+            const uint32_t qa = smem_addr(smem + L::SM_Q), qa_lo = smem_addr(smem + L::SM_QLO);
+            const uint32_t ring = smem_addr(smem + L::SM_RING);
             int seq = 0;
             auto take = [&](int &slot) -> bool {
-                slot = seq % PF_SLOTS;
-                if (!mbar_wait(full + slot, (seq / PF_SLOTS) & 1, abort_flag)) return false;
+                slot = seq % SLOTS;
+                if (!mbar_wait(full + slot, (seq / SLOTS) & 1, abort_flag)) return false;
                 tc_fence_after();
                 return true;
             };
@@ -161,15 +194,17 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 const int b = i & 1;
                 if (!mbar_wait(p_full + b, (i >> 1) & 1, abort_flag)) return false;
                 tc_fence_after();
+                const uint32_t pa = tmem + PF_TM_S + b * PF_BN;
                 for (int c = 0; c < 4; ++c) {
                     int slot;
                     if (!take(slot)) return false;
                     const uint32_t vb = ring + slot * PF_CHUNK;
 #pragma unroll
-                    for (int kk = 0; kk < 2; ++kk)
-                        mma_f16_ts(tmem + PF_TM_O, tmem + PF_TM_S + b * PF_BN + c * 16 + kk * 8,
-                                   sw128_desc(vb + kk * 16 * 128, 32 * 128, 1024), idesc_pv,
-                                   (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 2; ++kk) {
+                        const uint64_t vd = sw128_desc(vb + kk * 16 * 128, 32 * 128, 1024);
+                        mma_f16_ts(tmem + PF_TM_O, pa + c * 16 + kk * 8, vd, idesc_pv, (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
+                        if (PRECISE) mma_f16_ts(tmem + PF_TM_O, pa + PF_TM_PLO + c * 16 + kk * 8, vd, idesc_pv, 1u);
+                    }
                     mma_commit(empty + slot);
                     ++seq;
                 }
@@ -189,10 +224,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                     if (!take(slot)) { ok = false; break; }
                     const uint32_t kb = ring + slot * PF_CHUNK;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_f16_ss(tmem + PF_TM_S + b * PF_BN,
-                                   sw128_desc(qa + c * PF_CHUNK + kk * 32, 16, 1024),
-                                   sw128_desc(kb + kk * 32, 16, 1024), idesc_qk, (c > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t kd = sw128_desc(kb + kk * 32, 16, 1024);
+                        mma_f16_ss(tmem + PF_TM_S + b * PF_BN, sw128_desc(qa + c * PF_CHUNK + kk * 32, 16, 1024), kd,
+                                   idesc_qk, (c > 0 || kk > 0) ? 1u : 0u);
+                        if (PRECISE)
+                            mma_f16_ss(tmem + PF_TM_S + b * PF_BN, sw128_desc(qa_lo + c * PF_CHUNK + kk * 32, 16, 1024),
+                                       kd, idesc_qk, 1u);
+                    }
                     mma_commit(empty + slot);
                     ++seq;
                 }
@@ -264,7 +303,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 tmem_wait_st();
             }
             const float mref = m_use == -INFINITY ? 0.f : m_use;
-            uint32_t hp[32];
+            // fp16 probabilities of keys [64 wg, 64 wg + 64) as 32 half2 words
+            // (precise: hi = fp16(p) and lo = fp16(p - hi)).
+            uint32_t hp[32], lp[PRECISE ? 32 : 1];
             float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < 64; c += 2) {
@@ -272,14 +313,23 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 const float p1 = exp2_approx(fmaf(x[c + 1], PF_SCORE_LOG2, -mref));
                 const __half2 h2 = __floats2half2_rn(p0, p1);
                 hp[c / 2] = *reinterpret_cast<const uint32_t *>(&h2);
+                if (PRECISE) {
+                    const float2 back = __half22float2(h2);
+                    const __half2 l2 = __floats2half2_rn(p0 - back.x, p1 - back.y);
+                    lp[c / 2] = *reinterpret_cast<const uint32_t *>(&l2);
+                }
                 sp[(c >> 1) & 3] += p0 + p1;
             }
             l += (sp[0] + sp[1]) + (sp[2] + sp[3]);
-            // fp16 P of keys [64 wg, 64 wg + 64) into TMEM columns [32 wg, 32 wg + 32)
-            // of this S buffer.
+            // P of keys [64 wg, 64 wg + 64) into TMEM columns [32 wg, 32 wg + 32)
+            // of this S buffer, the lo halves 64 columns further.
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+            for (int c = 0; c < 2; ++c) {
                 tmem_st16(t_lane + PF_TM_S + b * PF_BN + wg * 32 + c * 16, *reinterpret_cast<const float(*)[16]>(hp + c * 16));
+                if (PRECISE)
+                    tmem_st16(t_lane + PF_TM_S + b * PF_BN + PF_TM_PLO + wg * 32 + c * 16,
+                              *reinterpret_cast<const float(*)[16]>(lp + c * 16));
+            }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -294,19 +344,20 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             ok = warp_wait_all(lbar, 0, abort_flag);
         }
         // Epilogue: the final PV's commit on p_free marks O complete (and every
-        // K/V chunk consumed, so the ring is idle). O leaves through shared
-        // memory: each lane puts its 128 columns into a padded staging row, then
-        // the warp stores each row's 512 bytes at once.
+        // MMA and K/V chunk done, so the query buffers and the ring are idle).
+        // O leaves through shared memory: each lane puts its 128 columns into a
+        // padded staging row, then the warp stores each row's 512 bytes at
+        // once, divided by the row sum and, with a gate, times sigmoid(gate).
         if (ok && ntiles > 0 &&
             warp_wait_all(p_free + ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag)) {
             tc_fence_after();
-            const float lt = lx[r] + lx[128 + r];
-            const float inv = lt > 0.f ? 1.f / lt : 0.f;
-            if (valid && wg == 0 && p.lse)
+            if (valid && wg == 0 && p.lse) {
+                const float lt = lx[r] + lx[128 + r];
                 p.lse[(size_t)t * PF_NQ + head] = lt > 0.f ? (m_use + log2f(lt)) * PF_LN2 : -INFINITY;
+            }
             constexpr int RS = 128 * 4 + 16;                            // staging row bytes (padded)
-            static_assert(8 * 32 * RS <= PF_SLOTS * PF_CHUNK, "O staging exceeds the ring");
-            uint8_t *stage = smem + PF_SM_RING + (warp - 4) * 32 * RS;
+            static_assert(8 * 32 * RS <= L::SM_XCH, "O staging exceeds the query buffers and the ring");
+            uint8_t *stage = smem + (warp - 4) * 32 * RS;
             uint8_t *myrow = stage + lane * RS;
 #pragma unroll
             for (int c4 = 0; c4 < 2; ++c4) {
@@ -319,14 +370,26 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
                     for (int e = 0; e < 16; e += 4)
                         *reinterpret_cast<float4 *>(myrow + (c4 * 64 + q * 16 + e) * 4) =
-                            make_float4(o[q][e] * inv, o[q][e + 1] * inv, o[q][e + 2] * inv, o[q][e + 3] * inv);
+                            make_float4(o[q][e], o[q][e + 1], o[q][e + 2], o[q][e + 3]);
             }
             __syncwarp();
-            const int nvalid = max(0, min(32, p.T - tok0 - wq * 32));    // valid rows are a prefix
+            const int row0 = wq * 32;
+            const int nvalid = max(0, min(32, p.T - tok0 - row0));      // valid rows are a prefix
 #pragma unroll 4
             for (int i = 0; i < nvalid; ++i) {
-                float *dst = p.out + ((size_t)(tok0 + wq * 32 + i) * PF_NQ + head) * PF_HD + wg * 128;
-                *reinterpret_cast<float4 *>(dst + 4 * lane) = *reinterpret_cast<const float4 *>(stage + i * RS + lane * 16);
+                const int tt = tok0 + row0 + i;
+                const float lt = lx[row0 + i] + lx[128 + row0 + i];
+                const float inv = lt > 0.f ? 1.f / lt : 0.f;
+                float4 v = *reinterpret_cast<const float4 *>(stage + i * RS + lane * 16);
+                v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
+                if (p.q_gate) {
+                    const float4 g = *reinterpret_cast<const float4 *>(
+                        p.q_gate + ((size_t)tt * PF_NQ + head) * 2 * PF_HD + PF_HD + wg * 128 + 4 * lane);
+                    v.x *= sigmoidf_(g.x); v.y *= sigmoidf_(g.y);
+                    v.z *= sigmoidf_(g.z); v.w *= sigmoidf_(g.w);
+                }
+                float *dst = p.out + ((size_t)tt * PF_NQ + head) * PF_HD + wg * 128;
+                *reinterpret_cast<float4 *>(dst + 4 * lane) = v;
             }
         }
     }
@@ -336,19 +399,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 pf_encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        cudaDriverEntryPointQueryResult q;
-        void *ptr = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess || !ptr)
-            throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
-        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }
-    return fn;
-}
-
 // 2-D fp16 map [rows][width] with 64-element x 'box_rows' boxes, 128B swizzle.
 CUtensorMap pf_map(const void *base, int width, int rows, int box_rows) {
     CUtensorMap m;
@@ -356,33 +406,51 @@ CUtensorMap pf_map(const void *base, int width, int rows, int box_rows) {
     cuuint64_t strides[1] = {(cuuint64_t)width * sizeof(__half)};
     cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    const CUresult r = pf_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides,
-                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
     return m;
 }
 
 PerDeviceOnce g_prefill_configured;
+
+template <bool PRECISE>
+void launch_prefill(float *out, float *lse, const float *q_gate, const __half *q, const __half *q_lo,
+                    const __half *kc, const __half *vc, int T, int position, int kv_rows, cudaStream_t st) {
+    g_prefill_configured.run([] {
+        if (cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PfLayout<false>::SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PfLayout<true>::SMEM_BYTES) != cudaSuccess)
+            throw std::runtime_error("cannot reserve shared memory for the prefill kernel");
+    });
+    if (T <= 0) return;
+    const CUtensorMap mq = pf_map(q, PF_NQ * PF_HD, T, PF_QROWS);
+    const CUtensorMap mql = PRECISE ? pf_map(q_lo, PF_NQ * PF_HD, T, PF_QROWS) : mq;
+    const CUtensorMap mk = pf_map(kc, PF_NKV * PF_HD, kv_rows, PF_BN);
+    const CUtensorMap mv = pf_map(vc, PF_NKV * PF_HD, kv_rows, 32);
+    PfParams p{out, lse, q_gate, T, position, kv_rows};
+    const cudaError_t e = launch_chained(prefill_kernel<PRECISE>, dim3(PF_NQ, (T + PF_QROWS - 1) / PF_QROWS),
+                                         dim3(384), PfLayout<PRECISE>::SMEM_BYTES, st, mq, mql, mk, mv, p);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("prefill attention launch: ") + cudaGetErrorString(e));
+}
 }  // namespace
 
 // Core-level causal prefill on already-prepared fp16 queries (no norm, RoPE
 // or gate): out [T][24][256] = softmax(q.k/16, causal) v, optional LSE.
 void prefill_core(float *out, float *lse, const __half *q, const __half *kc, const __half *vc, int T,
                   int position, cudaStream_t st) {
-    g_prefill_configured.run([] {
-        if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM_BYTES) !=
-            cudaSuccess)
-            throw std::runtime_error("cannot reserve shared memory for the prefill kernel");
-    });
-    const int kv_rows = position + T;
-    const CUtensorMap mq = pf_map(q, PF_NQ * PF_HD, T, PF_QROWS);
-    const CUtensorMap mk = pf_map(kc, PF_NKV * PF_HD, kv_rows, PF_BN);
-    const CUtensorMap mv = pf_map(vc, PF_NKV * PF_HD, kv_rows, 32);
-    PfParams p{out, lse, T, position, kv_rows};
-    const cudaError_t e = launch_chained(prefill_kernel, dim3(PF_NQ, (T + PF_QROWS - 1) / PF_QROWS), dim3(384),
-                                         PF_SMEM_BYTES, st, mq, mk, mv, p);
-    if (e != cudaSuccess) throw std::runtime_error(std::string("prefill attention launch: ") + cudaGetErrorString(e));
+    launch_prefill<false>(out, lse, nullptr, q, nullptr, kc, vc, T, position, position + T, st);
+}
+
+// The attention layer's prefill after its prepare step: queries as fp16 hi /
+// lo rows [T][24][256], cache rows [0, kv_rows) with token t seeing rows
+// [0, position + t] (position = cache row of token 0), out = the normalised
+// rows times sigmoid(gate) when q_gate is given.
+void prefill_precise(float *out, const __half *q, const __half *q_lo, const float *q_gate, const __half *kc,
+                     const __half *vc, int T, int position, int kv_rows, cudaStream_t st) {
+    launch_prefill<true>(out, nullptr, q_gate, q, q_lo, kc, vc, T, position, kv_rows, st);
 }
 
 }  // namespace qv

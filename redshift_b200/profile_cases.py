@@ -4,6 +4,7 @@
     python -m redshift_b200.profile_cases decode_exchange [context]  # the same through the peer exchange (1 rank)
     python -m redshift_b200.profile_cases delta   [tokens]    # one DeltaNet layer (16/48 heads, d128)
     python -m redshift_b200.profile_cases prefill [tokens]    # core causal prefill attention
+    python -m redshift_b200.profile_cases attention_prefill [tokens]  # attention layer, prefill regime
     python -m redshift_b200.profile_cases delta_core [tokens] # DeltaNet prefill recurrence (core)
     python -m redshift_b200.profile_cases delta_chunked [tokens] # DeltaNet prefill, chunked tcgen05 form
     python -m redshift_b200.profile_cases mm_q8_0 [rows]      # verify-8 projection, width 5120 (also mm_q4_k, mm_q6_k)
@@ -109,13 +110,25 @@ def make_case(hot, case, size):
         v = torch.randn((L, HKV, HD), generator=g, device=dev, dtype=torch.float16)
         out = torch.empty((L, H, HD), **f32)
         return lambda: hot.prefill_attention(out, q, k, v, L)
+    if case == 'attention_prefill':
+        # the attention layer's prefill regime: prepare (norms, rotary, append) + precise causal block
+        L = size or 4096
+        kc = torch.zeros((L, HKV, HD), device=dev, dtype=torch.float16)
+        vc = torch.zeros_like(kc)
+        qg = torch.randn((L, H, 2 * HD), generator=g, **f32)
+        key = torch.randn((L, HKV, HD), generator=g, **f32)
+        val = torch.randn((L, HKV, HD), generator=g, **f32)
+        ones = torch.ones(HD, **f32)
+        out = torch.empty((L, H, HD), **f32)
+        ws = torch.zeros(hot.lib.qv_attention_workspace(L, 0), dtype=torch.uint8, device=dev)
+        return lambda: hot.attention(out, kc, vc, qg, key, val, ones, ones, L, 0, workspace=ws)
     raise ValueError(f'unknown case {case}')
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument('case', choices=['decode', 'decode_exchange', 'delta', 'prefill', 'delta_core', 'delta_chunked',
-                                     'mm_q8_0', 'mm_q4_k', 'mm_q6_k'])
+    ap.add_argument('case', choices=['decode', 'decode_exchange', 'delta', 'prefill', 'attention_prefill', 'delta_core',
+                                     'delta_chunked', 'mm_q8_0', 'mm_q4_k', 'mm_q6_k'])
     ap.add_argument('size', type=int, nargs='?', default=0)
     ap.add_argument('--reps', type=int, default=3)
     ap.add_argument('--time', action='store_true')

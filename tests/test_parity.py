@@ -93,7 +93,7 @@ def test_attention_tile_edges(lib, position, batch):
 
 
 # ------------------------------------------------------------------ prefill (ABI level)
-@pytest.mark.parametrize('position,batch', [(0, 9), (100, 21), (37, 300), (0, 1000)])
+@pytest.mark.parametrize('position,batch', [(0, 9), (100, 21), (37, 300), (0, 1000), (4000, 130), (127, 64)])
 def test_attention_prefill_abi(lib, position, batch):
     c = I.attention_layer(batch=batch, position=position, seed=3000 + batch)
     exp_out, exp_k, exp_v = oracle.attention(**c)
