@@ -132,6 +132,15 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // L2 prefetch hints for the gate half-rows the epilogue multiplies by
+    // (softmax thread = query row; its warpgroup's 128 gate values, 4 lines).
+    if (warp >= 4 && p.q_gate && tok0 + (warp & 3) * 32 + lane < p.T) {
+        const float *g = p.q_gate + ((size_t)(tok0 + (warp & 3) * 32 + lane) * PF_NQ + head) * 2 * PF_HD + PF_HD +
+                         ((warp - 4) >> 2) * 128;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) prefetch_l2(g + 32 * k);
+    }
+
     // Everything below may read what the previous kernel of the stream wrote.
     grid_dependency_wait();
     if (threadIdx.x == 0) launch_dependents();
@@ -181,8 +190,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         if (lane == 0) {
             constexpr uint32_t idesc_qk = idesc_f16(128, PF_BN, false, false);
             constexpr uint32_t idesc_pv = idesc_f16(128, PF_HD, false, true);
-            const uint32_t qa = smem_addr(smem + L::SM_Q), qa_lo = smem_addr(smem + L::SM_QLO);
-            const uint32_t ring = smem_addr(smem + L::SM_RING);
+            // Operand descriptors: the base ones once, then the 16-byte units of
+            // an operand's offset added to the start-address field (shared
+            // addresses stay below 256 KB, so the 14-bit field cannot carry).
+            const uint64_t qd0 = sw128_desc(smem_addr(smem + L::SM_Q), 16, 1024);
+            const uint64_t qld0 = sw128_desc(smem_addr(smem + L::SM_QLO), 16, 1024);
+            const uint64_t kd0 = sw128_desc(smem_addr(smem + L::SM_RING), 16, 1024);
+            const uint64_t vd0 = sw128_desc(smem_addr(smem + L::SM_RING), 32 * 128, 1024);
             int seq = 0;
             auto take = [&](int &slot) -> bool {
                 slot = seq % SLOTS;
@@ -198,10 +212,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 for (int c = 0; c < 4; ++c) {
                     int slot;
                     if (!take(slot)) return false;
-                    const uint32_t vb = ring + slot * PF_CHUNK;
+                    const uint64_t vb = vd0 + (uint64_t)(slot * (PF_CHUNK >> 4));
 #pragma unroll
                     for (int kk = 0; kk < 2; ++kk) {
-                        const uint64_t vd = sw128_desc(vb + kk * 16 * 128, 32 * 128, 1024);
+                        const uint64_t vd = vb + (kk * 16 * 128 >> 4);
                         mma_f16_ts(tmem + PF_TM_O, pa + c * 16 + kk * 8, vd, idesc_pv, (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
                         if (PRECISE) mma_f16_ts(tmem + PF_TM_O, pa + PF_TM_PLO + c * 16 + kk * 8, vd, idesc_pv, 1u);
                     }
@@ -222,15 +236,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 for (int c = 0; c < 4 && ok; ++c) {
                     int slot;
                     if (!take(slot)) { ok = false; break; }
-                    const uint32_t kb = ring + slot * PF_CHUNK;
+                    const uint64_t kb = kd0 + (uint64_t)(slot * (PF_CHUNK >> 4));
+                    const uint32_t qo = (c * PF_CHUNK) >> 4;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t kd = sw128_desc(kb + kk * 32, 16, 1024);
-                        mma_f16_ss(tmem + PF_TM_S + b * PF_BN, sw128_desc(qa + c * PF_CHUNK + kk * 32, 16, 1024), kd,
-                                   idesc_qk, (c > 0 || kk > 0) ? 1u : 0u);
-                        if (PRECISE)
-                            mma_f16_ss(tmem + PF_TM_S + b * PF_BN, sw128_desc(qa_lo + c * PF_CHUNK + kk * 32, 16, 1024),
-                                       kd, idesc_qk, 1u);
+                        const uint64_t kd = kb + kk * 2;
+                        mma_f16_ss(tmem + PF_TM_S + b * PF_BN, qd0 + (uint64_t)(qo + kk * 2), kd, idesc_qk,
+                                   (c > 0 || kk > 0) ? 1u : 0u);
+                        if (PRECISE) mma_f16_ss(tmem + PF_TM_S + b * PF_BN, qld0 + (uint64_t)(qo + kk * 2), kd, idesc_qk, 1u);
                     }
                     mma_commit(empty + slot);
                     ++seq;
@@ -375,21 +388,35 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             __syncwarp();
             const int row0 = wq * 32;
             const int nvalid = max(0, min(32, p.T - tok0 - row0));      // valid rows are a prefix
-#pragma unroll 4
-            for (int i = 0; i < nvalid; ++i) {
-                const int tt = tok0 + row0 + i;
-                const float lt = lx[row0 + i] + lx[128 + row0 + i];
-                const float inv = lt > 0.f ? 1.f / lt : 0.f;
-                float4 v = *reinterpret_cast<const float4 *>(stage + i * RS + lane * 16);
-                v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
+            // Eight rows at a time, their gate values loaded before any of their
+            // stores (a load the compiler cannot move above an earlier store
+            // would otherwise cost one memory latency per row).
+            constexpr int RB = 8;
+            for (int i0 = 0; i0 < nvalid; i0 += RB) {
+                float4 g[RB];
                 if (p.q_gate) {
-                    const float4 g = *reinterpret_cast<const float4 *>(
-                        p.q_gate + ((size_t)tt * PF_NQ + head) * 2 * PF_HD + PF_HD + wg * 128 + 4 * lane);
-                    v.x *= sigmoidf_(g.x); v.y *= sigmoidf_(g.y);
-                    v.z *= sigmoidf_(g.z); v.w *= sigmoidf_(g.w);
+#pragma unroll
+                    for (int k = 0; k < RB; ++k)
+                        g[k] = i0 + k < nvalid ? *reinterpret_cast<const float4 *>(
+                                                     p.q_gate + ((size_t)(tok0 + row0 + i0 + k) * PF_NQ + head) * 2 * PF_HD +
+                                                     PF_HD + wg * 128 + 4 * lane)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                float *dst = p.out + ((size_t)tt * PF_NQ + head) * PF_HD + wg * 128;
-                *reinterpret_cast<float4 *>(dst + 4 * lane) = v;
+#pragma unroll
+                for (int k = 0; k < RB; ++k) {
+                    const int i = i0 + k;
+                    if (i >= nvalid) break;
+                    const float lt = lx[row0 + i] + lx[128 + row0 + i];
+                    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+                    float4 v = *reinterpret_cast<const float4 *>(stage + i * RS + lane * 16);
+                    v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
+                    if (p.q_gate) {
+                        v.x *= sigmoidf_(g[k].x); v.y *= sigmoidf_(g[k].y);
+                        v.z *= sigmoidf_(g[k].z); v.w *= sigmoidf_(g[k].w);
+                    }
+                    float *dst = p.out + ((size_t)(tok0 + row0 + i) * PF_NQ + head) * PF_HD + wg * 128;
+                    *reinterpret_cast<float4 *>(dst + 4 * lane) = v;
+                }
             }
         }
     }
