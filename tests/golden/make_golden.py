@@ -1,7 +1,8 @@
 """Generate golden vectors by running the reference's own CPU oracle.
 
-Run in a container where cristianku/redshift is checked out (default
-``/root/reference``; override with ``REDSHIFT_REFERENCE``)::
+Run in a container where cristianku/redshift is checked out (by default as
+``reference/`` beside this repository's checkout; override with
+``REDSHIFT_REFERENCE``)::
 
     python tests/golden/make_golden.py
 
@@ -26,7 +27,7 @@ from oracle import inputs as I  # noqa: E402
 
 
 def reference_module():
-    root = Path(os.environ.get('REDSHIFT_REFERENCE', '/root/reference'))
+    root = Path(os.environ.get('REDSHIFT_REFERENCE', HERE.parents[2] / 'reference'))
     sys.path.insert(0, str(root / 'tests'))
     import cpu_reference  # noqa: E402  (the reference's own oracle, unchanged)
     return cpu_reference

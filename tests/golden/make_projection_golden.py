@@ -1,8 +1,9 @@
 """Golden vectors for the quantized-projection oracle, made by the reference's
 own independent decoder.
 
-Run in a container where cristianku/redshift is checked out (default
-``/root/reference``; override with ``REDSHIFT_REFERENCE``)::
+Run in a container where cristianku/redshift is checked out (by default as
+``reference/`` beside this repository's checkout; override with
+``REDSHIFT_REFERENCE``)::
 
     python tests/golden/make_projection_golden.py
 
@@ -25,7 +26,7 @@ CASES = [(8, 512, 7), (8, 96, 7), (12, 512, 7), (12, 768, 3), (14, 512, 7), (14,
 
 
 def reference_test_module():
-    root = Path(os.environ.get('REDSHIFT_REFERENCE', '/root/reference'))
+    root = Path(os.environ.get('REDSHIFT_REFERENCE', HERE.parents[2] / 'reference'))
     sys.path.insert(0, str(root))
     sys.path.insert(0, str(root / 'tests'))
     import test_cuda  # noqa: E402  (the reference's own test module, unchanged)
