@@ -17,10 +17,11 @@
 // One CTA per (128 queries, query head), 384 threads:
 //  * warp 0: TMA producer. The CTA's query rows once (64 KB per fp16 half, four
 //    128B-swizzled 64-dim column chunks each), then the K and V tiles of 128
-//    keys as 16 KB chunks into a ring of slots, in the order the MMA warp
+//    keys as 32 KB chunks into a ring of slots, in the order the MMA warp
 //    consumes them: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1). A K chunk
-//    is 128 keys x 64 dims (one box), a V chunk 32 keys x 256 dims (four boxes
-//    of 64 dims).
+//    is 128 keys x 128 dims (two boxes of 64 dims), a V chunk 64 keys x 256
+//    dims (four boxes of 64 dims). Half-tile chunks keep the MMA thread's
+//    per-chunk waits, fences and commits at four per tile.
 //  * warp 1: MMA issuer. S_j = Q K_j^T as M=128 N=128 K=16 MMAs (16, or 32 in
 //    the precise form) into one of two 128-column TMEM buffers, then
 //    O += P_(j-1) V_(j-1) as M=128 N=256 MMAs (8, or 16) whose A operand, the
@@ -35,7 +36,7 @@
 //    row sum. Epilogue: warpgroup g writes O columns [128g, 128g+128).
 // TMEM: S buffers [0, 256), O [256, 512). A score buffer's probabilities take
 // its columns [0, 64) (fp16 pairs), the precise form's lo halves [64, 128).
-// Shared memory: Q 64 KB + a ring of ten slots, or Q hi + lo 128 KB + six.
+// Shared memory: Q 64 KB + a ring of five 32 KB slots, or Q hi + lo 128 KB + three.
 #include "common.cuh"
 #include "hotpath.h"
 
@@ -50,13 +51,14 @@ namespace {
 constexpr int PF_NQ = 24, PF_NKV = 4, PF_HD = 256, PF_GROUP = PF_NQ / PF_NKV;
 constexpr int PF_QROWS = 128;                  // queries per CTA
 constexpr int PF_BN = 128;                     // keys per tile
-constexpr int PF_CHUNK = 16384;                // bytes per ring slot, and per 64-dim query chunk
+constexpr int PF_QCHUNK = 16384;               // bytes per 64-dim query chunk [128 rows][128 B]
+constexpr int PF_CHUNK = 32768;                // bytes per ring slot: half a K or V tile
 template <bool PRECISE>
 struct PfLayout {
-    static constexpr int SLOTS = PRECISE ? 6 : 10;                  // ring slots
-    static constexpr int SM_Q = 0;                                  // 4 chunks of [128 rows][128 B]
-    static constexpr int SM_QLO = SM_Q + 4 * PF_CHUNK;              // precise: the lo halves, 4 chunks
-    static constexpr int SM_RING = SM_Q + (PRECISE ? 8 : 4) * PF_CHUNK;
+    static constexpr int SLOTS = PRECISE ? 3 : 5;                   // ring slots
+    static constexpr int SM_Q = 0;                                  // 4 query chunks
+    static constexpr int SM_QLO = SM_Q + 4 * PF_QCHUNK;             // precise: the lo halves, 4 chunks
+    static constexpr int SM_RING = SM_Q + (PRECISE ? 8 : 4) * PF_QCHUNK;
     static constexpr int SM_XCH = SM_RING + SLOTS * PF_CHUNK;       // [2 buffers][2 warpgroups][128 rows] floats
     static constexpr int SM_BAR = SM_XCH + 2 * 2 * 128 * 4;
     static constexpr int SMEM_BYTES = SM_BAR + 256;
@@ -148,11 +150,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            mbar_expect_tx(q_full, (PRECISE ? 8 : 4) * PF_CHUNK);
+            mbar_expect_tx(q_full, (PRECISE ? 8 : 4) * PF_QCHUNK);
             for (int c = 0; c < 4; ++c) {
-                tma_load_2d(smem + L::SM_Q + c * PF_CHUNK, &tmQ, q_full, head * PF_HD + c * 64, tok0);
+                tma_load_2d(smem + L::SM_Q + c * PF_QCHUNK, &tmQ, q_full, head * PF_HD + c * 64, tok0);
                 if (PRECISE)
-                    tma_load_2d(smem + L::SM_QLO + c * PF_CHUNK, &tmQlo, q_full, head * PF_HD + c * 64, tok0);
+                    tma_load_2d(smem + L::SM_QLO + c * PF_QCHUNK, &tmQlo, q_full, head * PF_HD + c * 64, tok0);
             }
             int seq = 0;
             bool ok = true;
@@ -165,17 +167,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 if (s == 0) { is_k = true; tile = 0; }
                 else if (s & 1) { tile = (s + 1) / 2; is_k = tile < ntiles; if (!is_k) tile = ntiles - 1; }
                 else { is_k = false; tile = s / 2 - 1; }
-                for (int c = 0; c < 4 && ok; ++c, ++seq) {
+                for (int c = 0; c < 2 && ok; ++c, ++seq) {
                     const int slot = seq % SLOTS;
                     if (seq >= SLOTS && !mbar_wait(empty + slot, ((seq / SLOTS) - 1) & 1, abort_flag)) { ok = false; break; }
                     uint8_t *dst = smem + L::SM_RING + slot * PF_CHUNK;
                     mbar_expect_tx(full + slot, PF_CHUNK);
-                    if (is_k) {
-                        tma_load_2d(dst, &tmK, full + slot, kv_head * PF_HD + c * 64, tile * PF_BN);
-                    } else {
+                    if (is_k) {                 // dims [128c, 128c + 128) of the tile's 128 keys
+#pragma unroll
+                        for (int e = 0; e < 2; ++e)
+                            tma_load_2d(dst + e * 16384, &tmK, full + slot, kv_head * PF_HD + c * 128 + e * 64, tile * PF_BN);
+                    } else {                    // keys [64c, 64c + 64), all 256 dims
 #pragma unroll
                         for (int d = 0; d < 4; ++d)
-                            tma_load_2d(dst + d * 4096, &tmV, full + slot, kv_head * PF_HD + d * 64, tile * PF_BN + c * 32);
+                            tma_load_2d(dst + d * 8192, &tmV, full + slot, kv_head * PF_HD + d * 64, tile * PF_BN + c * 64);
                     }
                 }
             }
@@ -196,7 +200,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             const uint64_t qd0 = sw128_desc(smem_addr(smem + L::SM_Q), 16, 1024);
             const uint64_t qld0 = sw128_desc(smem_addr(smem + L::SM_QLO), 16, 1024);
             const uint64_t kd0 = sw128_desc(smem_addr(smem + L::SM_RING), 16, 1024);
-            const uint64_t vd0 = sw128_desc(smem_addr(smem + L::SM_RING), 32 * 128, 1024);
+            const uint64_t vd0 = sw128_desc(smem_addr(smem + L::SM_RING), 64 * 128, 1024);
             int seq = 0;
             auto take = [&](int &slot) -> bool {
                 slot = seq % SLOTS;
@@ -209,15 +213,15 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 if (!mbar_wait(p_full + b, (i >> 1) & 1, abort_flag)) return false;
                 tc_fence_after();
                 const uint32_t pa = tmem + PF_TM_S + b * PF_BN;
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     int slot;
                     if (!take(slot)) return false;
                     const uint64_t vb = vd0 + (uint64_t)(slot * (PF_CHUNK >> 4));
 #pragma unroll
-                    for (int kk = 0; kk < 2; ++kk) {
+                    for (int kk = 0; kk < 4; ++kk) {      // keys [64c + 16kk, +16)
                         const uint64_t vd = vb + (kk * 16 * 128 >> 4);
-                        mma_f16_ts(tmem + PF_TM_O, pa + c * 16 + kk * 8, vd, idesc_pv, (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
-                        if (PRECISE) mma_f16_ts(tmem + PF_TM_O, pa + PF_TM_PLO + c * 16 + kk * 8, vd, idesc_pv, 1u);
+                        mma_f16_ts(tmem + PF_TM_O, pa + c * 32 + kk * 8, vd, idesc_pv, (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
+                        if (PRECISE) mma_f16_ts(tmem + PF_TM_O, pa + PF_TM_PLO + c * 32 + kk * 8, vd, idesc_pv, 1u);
                     }
                     mma_commit(empty + slot);
                     ++seq;
@@ -233,17 +237,21 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 // (issued earlier by this thread, after the softmax released
                 // them) reads before this QK overwrites them: MMAs issued by
                 // one thread execute in order.
-                for (int c = 0; c < 4 && ok; ++c) {
+                for (int c = 0; c < 2 && ok; ++c) {
                     int slot;
                     if (!take(slot)) { ok = false; break; }
                     const uint64_t kb = kd0 + (uint64_t)(slot * (PF_CHUNK >> 4));
-                    const uint32_t qo = (c * PF_CHUNK) >> 4;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t kd = kb + kk * 2;
-                        mma_f16_ss(tmem + PF_TM_S + b * PF_BN, qd0 + (uint64_t)(qo + kk * 2), kd, idesc_qk,
-                                   (c > 0 || kk > 0) ? 1u : 0u);
-                        if (PRECISE) mma_f16_ss(tmem + PF_TM_S + b * PF_BN, qld0 + (uint64_t)(qo + kk * 2), kd, idesc_qk, 1u);
+                    for (int e = 0; e < 2; ++e) {              // dims [128c + 64e, +64): query chunk 2c + e
+                        const uint32_t qo = ((2 * c + e) * PF_QCHUNK) >> 4;
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint64_t kd = kb + (uint64_t)((e * 16384) >> 4) + kk * 2;
+                            mma_f16_ss(tmem + PF_TM_S + b * PF_BN, qd0 + (uint64_t)(qo + kk * 2), kd, idesc_qk,
+                                       (c > 0 || e > 0 || kk > 0) ? 1u : 0u);
+                            if (PRECISE)
+                                mma_f16_ss(tmem + PF_TM_S + b * PF_BN, qld0 + (uint64_t)(qo + kk * 2), kd, idesc_qk, 1u);
+                        }
                     }
                     mma_commit(empty + slot);
                     ++seq;
@@ -457,7 +465,7 @@ void launch_prefill(float *out, float *lse, const float *q_gate, const __half *q
     const CUtensorMap mq = pf_map(q, PF_NQ * PF_HD, T, PF_QROWS);
     const CUtensorMap mql = PRECISE ? pf_map(q_lo, PF_NQ * PF_HD, T, PF_QROWS) : mq;
     const CUtensorMap mk = pf_map(kc, PF_NKV * PF_HD, kv_rows, PF_BN);
-    const CUtensorMap mv = pf_map(vc, PF_NKV * PF_HD, kv_rows, 32);
+    const CUtensorMap mv = pf_map(vc, PF_NKV * PF_HD, kv_rows, 64);
     PfParams p{out, lse, q_gate, T, position, kv_rows};
     const cudaError_t e = launch_chained(prefill_kernel<PRECISE>, dim3(PF_NQ, (T + PF_QROWS - 1) / PF_QROWS),
                                          dim3(384), PfLayout<PRECISE>::SMEM_BYTES, st, mq, mql, mk, mv, p);
