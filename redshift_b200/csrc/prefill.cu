@@ -17,11 +17,12 @@
 // One CTA per (128 queries, query head), 384 threads:
 //  * warp 0: TMA producer. The CTA's query rows once (64 KB per fp16 half, four
 //    128B-swizzled 64-dim column chunks each), then the K and V tiles of 128
-//    keys as 32 KB chunks into a ring of slots, in the order the MMA warp
-//    consumes them: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1). A K chunk
-//    is 128 keys x 128 dims (two boxes of 64 dims), a V chunk 64 keys x 256
-//    dims (four boxes of 64 dims). Half-tile chunks keep the MMA thread's
-//    per-chunk waits, fences and commits at four per tile.
+//    keys as chunks into a ring of slots, in the order the MMA warp consumes
+//    them: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1). Plain: a chunk is a
+//    whole 64 KB K or V tile (two slots); precise: half a tile, 32 KB (three
+//    slots), a K chunk 128 keys x 128 dims, a V chunk 64 keys x 256 dims. The
+//    MMA thread's per-chunk wait, fence and commit cost more than its MMAs at
+//    16 KB chunks, hence the large ones.
 //  * warp 1: MMA issuer. S_j = Q K_j^T as M=128 N=128 K=16 MMAs (16, or 32 in
 //    the precise form) into one of two 128-column TMEM buffers, then
 //    O += P_(j-1) V_(j-1) as M=128 N=256 MMAs (8, or 16) whose A operand, the
@@ -36,7 +37,8 @@
 //    row sum. Epilogue: warpgroup g writes O columns [128g, 128g+128).
 // TMEM: S buffers [0, 256), O [256, 512). A score buffer's probabilities take
 // its columns [0, 64) (fp16 pairs), the precise form's lo halves [64, 128).
-// Shared memory: Q 64 KB + a ring of five 32 KB slots, or Q hi + lo 128 KB + three.
+// Shared memory: Q 64 KB + a ring of two 64 KB slots, or Q hi + lo 128 KB + three
+// 32 KB slots.
 #include "common.cuh"
 #include "hotpath.h"
 
@@ -52,14 +54,15 @@ constexpr int PF_NQ = 24, PF_NKV = 4, PF_HD = 256, PF_GROUP = PF_NQ / PF_NKV;
 constexpr int PF_QROWS = 128;                  // queries per CTA
 constexpr int PF_BN = 128;                     // keys per tile
 constexpr int PF_QCHUNK = 16384;               // bytes per 64-dim query chunk [128 rows][128 B]
-constexpr int PF_CHUNK = 32768;                // bytes per ring slot: half a K or V tile
 template <bool PRECISE>
 struct PfLayout {
-    static constexpr int SLOTS = PRECISE ? 3 : 5;                   // ring slots
+    static constexpr int CPT = PRECISE ? 2 : 1;                     // ring chunks per K or V tile
+    static constexpr int CHUNK = 65536 / CPT;                       // bytes per ring slot
+    static constexpr int SLOTS = PRECISE ? 3 : 2;                   // ring slots
     static constexpr int SM_Q = 0;                                  // 4 query chunks
     static constexpr int SM_QLO = SM_Q + 4 * PF_QCHUNK;             // precise: the lo halves, 4 chunks
     static constexpr int SM_RING = SM_Q + (PRECISE ? 8 : 4) * PF_QCHUNK;
-    static constexpr int SM_XCH = SM_RING + SLOTS * PF_CHUNK;       // [2 buffers][2 warpgroups][128 rows] floats
+    static constexpr int SM_XCH = SM_RING + SLOTS * CHUNK;          // [2 buffers][2 warpgroups][128 rows] floats
     static constexpr int SM_BAR = SM_XCH + 2 * 2 * 128 * 4;
     static constexpr int SMEM_BYTES = SM_BAR + 256;
     static_assert(SMEM_BYTES <= 227 * 1024, "prefill kernel exceeds the shared memory of a CTA");
@@ -88,7 +91,8 @@ __global__ void __launch_bounds__(384, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmQlo,
                const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const PfParams p) {
     using L = PfLayout<PRECISE>;
-    constexpr int SLOTS = L::SLOTS;
+    constexpr int SLOTS = L::SLOTS, CPT = L::CPT, CHUNK = L::CHUNK;
+    constexpr int DPC = PF_HD / CPT, KPC = PF_BN / CPT;          // K dims / V keys per chunk
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023) {           // 128B-swizzle atoms need a 1024-byte aligned base
         if (threadIdx.x == 0) raise_status(STATUS_BAD_ARGUMENT);
@@ -167,19 +171,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 if (s == 0) { is_k = true; tile = 0; }
                 else if (s & 1) { tile = (s + 1) / 2; is_k = tile < ntiles; if (!is_k) tile = ntiles - 1; }
                 else { is_k = false; tile = s / 2 - 1; }
-                for (int c = 0; c < 2 && ok; ++c, ++seq) {
+                for (int c = 0; c < CPT && ok; ++c, ++seq) {
                     const int slot = seq % SLOTS;
                     if (seq >= SLOTS && !mbar_wait(empty + slot, ((seq / SLOTS) - 1) & 1, abort_flag)) { ok = false; break; }
-                    uint8_t *dst = smem + L::SM_RING + slot * PF_CHUNK;
-                    mbar_expect_tx(full + slot, PF_CHUNK);
-                    if (is_k) {                 // dims [128c, 128c + 128) of the tile's 128 keys
+                    uint8_t *dst = smem + L::SM_RING + slot * CHUNK;
+                    mbar_expect_tx(full + slot, CHUNK);
+                    if (is_k) {                 // dims [DPC c, DPC c + DPC) of the tile's 128 keys
 #pragma unroll
-                        for (int e = 0; e < 2; ++e)
-                            tma_load_2d(dst + e * 16384, &tmK, full + slot, kv_head * PF_HD + c * 128 + e * 64, tile * PF_BN);
-                    } else {                    // keys [64c, 64c + 64), all 256 dims
+                        for (int e = 0; e < DPC / 64; ++e)
+                            tma_load_2d(dst + e * 16384, &tmK, full + slot, kv_head * PF_HD + c * DPC + e * 64, tile * PF_BN);
+                    } else {                    // keys [KPC c, KPC c + KPC), all 256 dims
 #pragma unroll
                         for (int d = 0; d < 4; ++d)
-                            tma_load_2d(dst + d * 8192, &tmV, full + slot, kv_head * PF_HD + d * 64, tile * PF_BN + c * 64);
+                            tma_load_2d(dst + d * KPC * 128, &tmV, full + slot, kv_head * PF_HD + d * 64, tile * PF_BN + c * KPC);
                     }
                 }
             }
@@ -200,7 +204,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             const uint64_t qd0 = sw128_desc(smem_addr(smem + L::SM_Q), 16, 1024);
             const uint64_t qld0 = sw128_desc(smem_addr(smem + L::SM_QLO), 16, 1024);
             const uint64_t kd0 = sw128_desc(smem_addr(smem + L::SM_RING), 16, 1024);
-            const uint64_t vd0 = sw128_desc(smem_addr(smem + L::SM_RING), 64 * 128, 1024);
+            const uint64_t vd0 = sw128_desc(smem_addr(smem + L::SM_RING), KPC * 128, 1024);
             int seq = 0;
             auto take = [&](int &slot) -> bool {
                 slot = seq % SLOTS;
@@ -213,15 +217,16 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 if (!mbar_wait(p_full + b, (i >> 1) & 1, abort_flag)) return false;
                 tc_fence_after();
                 const uint32_t pa = tmem + PF_TM_S + b * PF_BN;
-                for (int c = 0; c < 2; ++c) {
+                for (int c = 0; c < CPT; ++c) {
                     int slot;
                     if (!take(slot)) return false;
-                    const uint64_t vb = vd0 + (uint64_t)(slot * (PF_CHUNK >> 4));
+                    const uint64_t vb = vd0 + (uint64_t)(slot * (CHUNK >> 4));
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {      // keys [64c + 16kk, +16)
+                    for (int kk = 0; kk < KPC / 16; ++kk) {      // keys [KPC c + 16kk, +16)
                         const uint64_t vd = vb + (kk * 16 * 128 >> 4);
-                        mma_f16_ts(tmem + PF_TM_O, pa + c * 32 + kk * 8, vd, idesc_pv, (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
-                        if (PRECISE) mma_f16_ts(tmem + PF_TM_O, pa + PF_TM_PLO + c * 32 + kk * 8, vd, idesc_pv, 1u);
+                        mma_f16_ts(tmem + PF_TM_O, pa + c * (KPC / 2) + kk * 8, vd, idesc_pv,
+                                   (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
+                        if (PRECISE) mma_f16_ts(tmem + PF_TM_O, pa + PF_TM_PLO + c * (KPC / 2) + kk * 8, vd, idesc_pv, 1u);
                     }
                     mma_commit(empty + slot);
                     ++seq;
@@ -237,13 +242,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 // (issued earlier by this thread, after the softmax released
                 // them) reads before this QK overwrites them: MMAs issued by
                 // one thread execute in order.
-                for (int c = 0; c < 2 && ok; ++c) {
+                for (int c = 0; c < CPT && ok; ++c) {
                     int slot;
                     if (!take(slot)) { ok = false; break; }
-                    const uint64_t kb = kd0 + (uint64_t)(slot * (PF_CHUNK >> 4));
+                    const uint64_t kb = kd0 + (uint64_t)(slot * (CHUNK >> 4));
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) {              // dims [128c + 64e, +64): query chunk 2c + e
-                        const uint32_t qo = ((2 * c + e) * PF_QCHUNK) >> 4;
+                    for (int e = 0; e < DPC / 64; ++e) {       // dims [DPC c + 64e, +64): query chunk
+                        const uint32_t qo = ((c * (DPC / 64) + e) * PF_QCHUNK) >> 4;
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
                             const uint64_t kd = kb + (uint64_t)((e * 16384) >> 4) + kk * 2;
@@ -465,7 +470,7 @@ void launch_prefill(float *out, float *lse, const float *q_gate, const __half *q
     const CUtensorMap mq = pf_map(q, PF_NQ * PF_HD, T, PF_QROWS);
     const CUtensorMap mql = PRECISE ? pf_map(q_lo, PF_NQ * PF_HD, T, PF_QROWS) : mq;
     const CUtensorMap mk = pf_map(kc, PF_NKV * PF_HD, kv_rows, PF_BN);
-    const CUtensorMap mv = pf_map(vc, PF_NKV * PF_HD, kv_rows, 64);
+    const CUtensorMap mv = pf_map(vc, PF_NKV * PF_HD, kv_rows, PF_BN / PfLayout<PRECISE>::CPT);
     PfParams p{out, lse, q_gate, T, position, kv_rows};
     const cudaError_t e = launch_chained(prefill_kernel<PRECISE>, dim3(PF_NQ, (T + PF_QROWS - 1) / PF_QROWS),
                                          dim3(384), PfLayout<PRECISE>::SMEM_BYTES, st, mq, mql, mk, mv, p);
